@@ -1,0 +1,115 @@
+/*
+ * hgemm_sm100.h - C ABI of the B200 (sm_100a) FP16 HGEMM library.
+ *
+ *   C[M,N] = A[M,K] @ B[K,N]   FP16 inputs, FP32 accumulation, FP16 output,
+ *                              row-major, alpha = 1, beta = 0.
+ *
+ * This is the boundary between host code (the llm_hgemm pybind11 module, or
+ * any other FFI) and the hand-written sm_100a kernels. It takes plain device
+ * pointers, sizes and a stream; no C++ exceptions and no torch types cross it.
+ *
+ * It replaces the reference's torch-typed launcher layer:
+ *   - csrc/kernels.h:6-78 and csrc/references/reference.h:13-29
+ *     (`void launch_X(const Tensor& a, const Tensor& b, Tensor& out,
+ *      cudaStream_t)`, one per backend)                -> hgemm_sm100_run
+ *   - csrc/dispatch.cpp:30-32 (`auto` -> backend) and :58-95 (name -> launcher
+ *     chain)                       -> hgemm_sm100_config_from_name / _resolve
+ *   - csrc/dispatch.cpp:104-128 (`backend_info`)  -> hgemm_sm100_workspace_bytes
+ *   - csrc/dispatch.cpp:99-101 (`has_cutlass`)    -> no counterpart (always 0)
+ * Input validation with the reference's messages (csrc/contract.cpp:3-22)
+ * stays in the host module; this layer re-checks sizes, strides and
+ * alignment and reports violations as status codes.
+ *
+ * Threading: every entry point is thread-safe. Launches are asynchronous on
+ * the given stream; nothing synchronises the host.
+ */
+#ifndef HGEMM_SM100_H_
+#define HGEMM_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (return value of every int-returning entry point). */
+enum {
+    HGEMM_SM100_OK = 0,
+    HGEMM_SM100_ERR_INVALID_ARGUMENT = 1,  /* null pointer, size <= 0, ld < row */
+    HGEMM_SM100_ERR_UNKNOWN_CONFIG = 2,    /* config id out of range            */
+    HGEMM_SM100_ERR_UNSUPPORTED_DEVICE = 3,/* current device is not sm_100      */
+    HGEMM_SM100_ERR_LAUNCH = 4,            /* CUDA launch / attribute failure   */
+    HGEMM_SM100_ERR_PIPELINE_TIMEOUT = 5,  /* a kernel wait ran out (status word)*/
+    HGEMM_SM100_ERR_TENSOR_MAP = 6,        /* cuTensorMapEncodeTiled failed     */
+    HGEMM_SM100_ERR_CUDA = 7               /* other CUDA runtime error          */
+};
+
+/* Kernel configurations. Every name is also accepted by
+ * hgemm_sm100_config_from_name (the `implementation=` strings of llm_hgemm). */
+enum {
+    HGEMM_SM100_CFG_AUTO = 0,              /* "auto": shape heuristic           */
+    HGEMM_SM100_CFG_PERSISTENT_128x256 = 1,/* "tc_persistent_128x256"           */
+    HGEMM_SM100_CFG_PERSISTENT_128x128 = 2,/* "tc_persistent_128x128"           */
+    HGEMM_SM100_CFG_SPLITK_128x128 = 3,    /* "tc_splitk_128x128": cluster split-K */
+    HGEMM_SM100_CFG_SWAPAB = 4,            /* "tc_swapab": C^T = B^T A^T, M <= 256 */
+    HGEMM_SM100_CFG_GENERIC_128x128 = 5,   /* "tc_generic_128x128": no TMA       */
+    HGEMM_SM100_CFG_COUNT = 6
+};
+
+/* Flags. */
+enum {
+    HGEMM_SM100_FLAG_OUT_F32 = 1,          /* C is FP32 (tensor-parallel partials) */
+    HGEMM_SM100_FLAG_TEST_INJECT_TX = 2    /* test only: arm one stage with 16 bytes
+                                              more than TMA delivers, so that the
+                                              pipeline wait runs out */
+};
+
+typedef struct HgemmSm100Args {
+    const void* a;       /* FP16 [m x lda], row-major, device memory          */
+    const void* b;       /* FP16 [k x ldb], row-major                         */
+    void* c;             /* FP16 (or FP32 with FLAG_OUT_F32) [m x ldc]        */
+    int64_t m, n, k;     /* > 0, each < 2^31                                   */
+    int64_t lda, ldb, ldc;  /* leading dimensions in elements (>= k, n, n)    */
+    int32_t config;      /* HGEMM_SM100_CFG_*                                 */
+    int32_t split_k;     /* 0 = choose; else K splits (1..16), split configs  */
+    int32_t flags;       /* HGEMM_SM100_FLAG_*                                */
+    int32_t* status;     /* optional device int32 the kernel sets on a pipeline
+                            timeout; NULL = the library's own status word     */
+    uint64_t timeout_ns; /* per-wait limit inside the kernel; 0 = 2 s          */
+} HgemmSm100Args;
+
+/* Launches C = A @ B on `stream` (a cudaStream_t; NULL = legacy default) on
+ * the current device. Explicit TMA configurations whose operands TMA cannot
+ * describe (a base not 16-byte aligned, or lda / ldb not a multiple of 8) run
+ * the generic configuration instead, as the reference's v6 kernels fall back
+ * to v5 (csrc/v6_mma_async.cu:428-437). Returns HGEMM_SM100_OK or an error;
+ * device-side pipeline timeouts are reported through the status word. */
+int hgemm_sm100_run(const HgemmSm100Args* args, void* stream);
+
+/* The configuration and K split that hgemm_sm100_run would launch for
+ * `args` (after `auto` resolution and the alignment fallback). */
+int hgemm_sm100_resolve(const HgemmSm100Args* args, int32_t* config_out, int32_t* split_out);
+
+/* Name <-> id of a configuration; unknown names give -1, unknown ids NULL. */
+int32_t hgemm_sm100_config_from_name(const char* name);
+const char* hgemm_sm100_config_name(int32_t config);
+int32_t hgemm_sm100_num_configs(void);
+
+/* Global-memory workspace a configuration needs: always 0 (split-K partials
+ * are reduced through distributed shared memory). Counterpart of
+ * backend_info()["workspace_bytes"] (reference csrc/dispatch.cpp:104-128). */
+size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k);
+
+/* Human-readable text of a status code. */
+const char* hgemm_sm100_status_string(int status);
+
+/* Reads (and with clear != 0 resets) the library's own device status word of
+ * the current device. Synchronises the device; for tests and debugging. */
+int hgemm_sm100_read_status(int32_t* value, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HGEMM_SM100_H_ */

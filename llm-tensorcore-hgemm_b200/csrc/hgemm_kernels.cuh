@@ -1,0 +1,578 @@
+// sm_100a HGEMM kernels: C[M,N] = A[M,K] @ B[K,N], FP16 in, FP32 accumulate
+// in TMEM, FP16 out, all row-major, alpha = 1, beta = 0.
+//
+// They replace the reference's kernel family (csrc/v1..v6 of the reference;
+// its best, mma_async_kernel in csrc/v6_mma_async.cu:226-403, is a two-stage
+// cp.async + mma.sync pipeline). Two kernels cover every shape:
+//
+//  * hgemm_persistent_kernel: one CTA per SM walks 128 x BN output tiles in
+//    grouped raster order. Warp 4 streams A/B tiles with TMA into a STAGES-deep
+//    shared-memory ring (full/empty mbarriers), one thread of warp 5 issues
+//    tcgen05.mma into one of two TMEM accumulators, warps 0-3 drain the other
+//    accumulator (tcgen05.ld -> FP16 -> global) while the next tile's MMAs run.
+//
+//  * hgemm_tile_kernel: one output tile per CTA, optionally split over K across
+//    the CTAs of a thread-block cluster whose FP32 partials are summed in a
+//    fixed order through distributed shared memory (no global workspace).
+//    kSwap computes C^T = B^T A^T so that a few activation rows (decode) sit
+//    on the MMA's N side while 128 weight columns fill the MMA's M side.
+//    kTma = false replaces TMA with predicated element loads by warps 0-3 for
+//    operands whose strides or base addresses TMA cannot describe (the role
+//    the reference gives its v5 scalar fallback, csrc/v6_mma_async.cu:428-437).
+//
+// Operand tiles in shared memory use the 128-byte swizzle that TMA writes:
+//  * the K-major tile ("Kmaj", from a row-major [rows x K] matrix) holds rows
+//    of 64 halves of K, 128 bytes each;
+//  * the MN-major tile ("MNmaj", from a row-major [K x cols] matrix) holds
+//    64-wide column chunks, each 64 K-rows of 128 bytes (8 KiB per chunk).
+// Every mbarrier wait is bounded; when one runs out the CTA records
+// HGEMM_SM100_ERR_PIPELINE_TIMEOUT in the status word, all roles give up,
+// in-flight copies and MMAs are drained (also bounded) and TMEM is freed.
+#pragma once
+
+#include "sm100_ptx.cuh"
+
+namespace hgemm {
+
+constexpr int kBlockK = 64;            // K per pipeline stage (one 128-byte swizzle row)
+constexpr int kMmaM = 128;             // UMMA M (rows of the accumulator = TMEM lanes)
+constexpr int kThreads = 192;          // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer
+constexpr uint32_t kChunkBytes = 64u * 128u;  // one 64-wide MN-major chunk of a stage
+constexpr uint64_t kDrainLimitNs = 200ull * 1000ull * 1000ull;
+
+__host__ __device__ constexpr uint32_t cmax(uint32_t a, uint32_t b) { return a > b ? a : b; }
+__host__ __device__ constexpr uint32_t tmem_cols_for(uint32_t n) {
+    return n <= 32 ? 32 : (n <= 64 ? 64 : (n <= 128 ? 128 : (n <= 256 ? 256 : 512)));
+}
+
+// Rounds the dynamic shared-memory window up to the 1024-byte alignment the
+// 128-byte swizzle atoms need.
+__device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
+    const uint32_t a = smem_addr(p);
+    return p + (((a + 1023u) & ~1023u) - a);
+}
+
+struct GemmParams {
+    const __half* a;       // [M, lda]
+    const __half* b;       // [K, ldb]
+    void* c;               // [M, ldc], FP16 (or FP32 when out_f32)
+    int m, n, k;
+    long long lda, ldb, ldc;
+    int vec_ok;            // C base 16-byte aligned and ldc % 8 == 0
+    int out_f32;           // store FP32 instead of FP16 (tensor-parallel partials)
+    int group_m;           // persistent kernel: M-tiles per raster group
+    int inject;            // test-only: arm the first stage with 16 extra bytes
+    int* status;
+    unsigned long long timeout_ns;
+};
+
+// ------------------------------------------------------------ epilogue ----
+
+// Stores `cnt` (16 or 32) consecutive accumulator columns of one output row.
+template <int kCnt>
+__device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, int col0,
+                                                  const uint32_t* v) {
+    if (row >= p.m) return;
+    if (p.out_f32) {
+        float* crow = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc;
+#pragma unroll
+        for (int i = 0; i < kCnt; ++i)
+            if (col0 + i < p.n) crow[col0 + i] = __uint_as_float(v[i]);
+        return;
+    }
+    __half* crow = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc;
+    if (p.vec_ok && col0 + kCnt <= p.n) {
+#pragma unroll
+        for (int i = 0; i < kCnt; i += 8) {
+            uint4 q;
+            q.x = pack_half2(v[i + 0], v[i + 1]);
+            q.y = pack_half2(v[i + 2], v[i + 3]);
+            q.z = pack_half2(v[i + 4], v[i + 5]);
+            q.w = pack_half2(v[i + 6], v[i + 7]);
+            *reinterpret_cast<uint4*>(crow + col0 + i) = q;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kCnt; ++i)
+            if (col0 + i < p.n) crow[col0 + i] = __float2half_rn(__uint_as_float(v[i]));
+    }
+}
+
+// Swapped tiles: accumulator row = output column `col`, accumulator columns =
+// output rows row0 .. row0 + cnt - 1.
+template <int kCnt>
+__device__ __forceinline__ void store_col_segment(const GemmParams& p, int col, int row0,
+                                                  const uint32_t* v) {
+    if (col >= p.n) return;
+#pragma unroll
+    for (int j = 0; j < kCnt; ++j) {
+        const int row = row0 + j;
+        if (row < p.m) {
+            const long long off = static_cast<long long>(row) * p.ldc + col;
+            if (p.out_f32) static_cast<float*>(p.c)[off] = __uint_as_float(v[j]);
+            else static_cast<__half*>(p.c)[off] = __float2half_rn(__uint_as_float(v[j]));
+        }
+    }
+}
+
+// Stores 4 consecutive output columns of one row from an FP32 quad.
+__device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col, float4 v) {
+    if (row >= p.m || col >= p.n) return;
+    const long long off = static_cast<long long>(row) * p.ldc + col;
+    if (p.out_f32) {
+        float* c = static_cast<float*>(p.c) + off;
+        if (p.vec_ok && col + 4 <= p.n) {
+            *reinterpret_cast<float4*>(c) = v;
+        } else {
+            c[0] = v.x;
+            if (col + 1 < p.n) c[1] = v.y;
+            if (col + 2 < p.n) c[2] = v.z;
+            if (col + 3 < p.n) c[3] = v.w;
+        }
+        return;
+    }
+    __half* c = static_cast<__half*>(p.c) + off;
+    if (p.vec_ok && col + 4 <= p.n) {
+        uint2 q;
+        q.x = pack_half2(__float_as_uint(v.x), __float_as_uint(v.y));
+        q.y = pack_half2(__float_as_uint(v.z), __float_as_uint(v.w));
+        *reinterpret_cast<uint2*>(c) = q;
+    } else {
+        c[0] = __float2half_rn(v.x);
+        if (col + 1 < p.n) c[1] = __float2half_rn(v.y);
+        if (col + 2 < p.n) c[2] = __float2half_rn(v.z);
+        if (col + 3 < p.n) c[3] = __float2half_rn(v.w);
+    }
+}
+
+// ------------------------------------------------- generic tile loaders ----
+
+// K-major tile: rows r0 .. r0 + kRows - 1 of the row-major [rows x K] matrix x,
+// K range k0 .. k0 + 63, zero outside the matrix. 128 cooperating threads.
+template <int kRows>
+__device__ __forceinline__ void load_kmaj_generic(uint8_t* dst, const __half* x, long long ldx,
+                                                  int rows, int kdim, int r0, int k0, int tid) {
+#pragma unroll 4
+    for (int idx = tid; idx < kRows * kBlockK; idx += 128) {
+        const int r = idx >> 6, kk = idx & 63;
+        const int gr = r0 + r, gk = k0 + kk;
+        __half v = __float2half_rn(0.f);
+        if (gr < rows && gk < kdim) v = x[static_cast<long long>(gr) * ldx + gk];
+        *reinterpret_cast<__half*>(dst + swz128(r, kk * 2)) = v;
+    }
+}
+
+// MN-major tile: columns c0 .. c0 + kCols - 1 of the row-major [K x cols]
+// matrix y, K range k0 .. k0 + 63, zero outside the matrix.
+template <int kCols>
+__device__ __forceinline__ void load_mnmaj_generic(uint8_t* dst, const __half* y, long long ldy,
+                                                   int kdim, int cols, int c0, int k0, int tid) {
+#pragma unroll 4
+    for (int idx = tid; idx < kCols * kBlockK; idx += 128) {
+        const int kk = idx / kCols, c = idx % kCols;
+        const int gk = k0 + kk, gc = c0 + c;
+        __half v = __float2half_rn(0.f);
+        if (gk < kdim && gc < cols) v = y[static_cast<long long>(gk) * ldy + gc];
+        *reinterpret_cast<__half*>(dst + (c >> 6) * kChunkBytes + swz128(kk, (c & 63) * 2)) = v;
+    }
+}
+
+// ---------------------------------------------------------- descriptors ----
+
+__device__ __forceinline__ uint64_t kmaj_desc(uint32_t tile, int kk) {
+    return make_smem_desc(tile + kk * 32u, 16u, 1024u);
+}
+__device__ __forceinline__ uint64_t mnmaj_desc(uint32_t tile, int kk) {
+    return make_smem_desc(tile + kk * 2048u, kChunkBytes, 1024u);
+}
+
+// Waits for the last armed phase of every used stage's full barrier, so that
+// no TMA write into this CTA's shared memory is still in flight at exit.
+template <int kStages>
+__device__ __forceinline__ void drain_tma(uint64_t* full, uint32_t issued) {
+    const uint32_t used = issued < kStages ? issued : kStages;
+    for (uint32_t s = 0; s < used; ++s) {
+        const uint32_t arms = issued / kStages + (s < issued % kStages ? 1u : 0u);
+        mbar_wait_drain(&full[s], (arms - 1u) & 1u, kDrainLimitNs);
+    }
+}
+
+// ========================================================== tile kernel ====
+
+template <int kBNm, bool kSwap, bool kTma, int kStages>
+struct TileCfg {
+    static constexpr int kKRows = kSwap ? kBNm : kMmaM;     // rows of the K-major tile
+    static constexpr int kMNCols = kSwap ? kMmaM : kBNm;    // cols of the MN-major tile
+    static constexpr uint32_t kKBytes = kKRows * 128u;
+    static constexpr uint32_t kMNBytes = kMNCols * 128u;
+    static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
+    // Split-K partial buffer (FP32), laid out so the output's contiguous
+    // dimension is contiguous: [row][col + 4 pad] or, swapped, [m][n].
+    static constexpr uint32_t kRedStride = kSwap ? kMmaM : (kBNm + 4);
+    static constexpr uint32_t kRedRows = kSwap ? kBNm : kMmaM;
+    static constexpr uint32_t kRedBytes = kRedRows * kRedStride * 4u;
+    static constexpr uint32_t kDataBytes = cmax(kStages * kStageBytes, kRedBytes);
+    static constexpr uint32_t kBarBytes = 256;
+    static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
+    static constexpr uint32_t kTmemCols = tmem_cols_for(kBNm);
+    static constexpr uint32_t kIdesc = make_idesc_f16(kMmaM, kBNm, kSwap, !kSwap);
+    static constexpr int kChunk = kBNm >= 32 ? 32 : 16;     // columns per tcgen05.ld
+    static_assert(kKRows % 8 == 0, "K-major tile rows must fill 8-row swizzle atoms");
+    static_assert(kMNCols % 64 == 0, "MN-major tile must be whole 64-wide chunks");
+    static_assert(kBNm % 16 == 0 && kBNm >= 16 && kBNm <= 256, "UMMA N for M=128");
+    static_assert(2 * kStages + 2 <= 30, "barrier area");
+    static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+// Grid: x = 128-row accumulator tiles (M tiles, or N tiles when swapped),
+// y = kBNm-wide accumulator column tiles, z = K splits (== cluster size).
+template <int kBNm, bool kSwap, bool kTma, int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_mn,
+                  const GemmParams p) {
+    using Cfg = TileCfg<kBNm, kSwap, kTma, kStages>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align_1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* drain = tfull + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_index();
+    const uint32_t lane = threadIdx.x & 31u;
+
+    if (warp == 4 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], kTma ? 1u : 128u);
+            mbar_init(&empty[s], 1u);
+        }
+        mbar_init(tfull, 1u);
+        mbar_init(drain, 1u);
+        *abort_flag = 0;
+        mbar_init_fence();
+        if (kTma) {
+            tma_prefetch_map(&tm_k);
+            tma_prefetch_map(&tm_mn);
+        }
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+    const int acc_row0 = blockIdx.x * kMmaM;   // accumulator rows (M, or N when swapped)
+    const int acc_col0 = blockIdx.y * kBNm;    // accumulator cols (N, or M when swapped)
+    const int k_rows0 = kSwap ? acc_col0 : acc_row0;   // first A row of the K-major tile
+    const int mn_cols0 = kSwap ? acc_row0 : acc_col0;  // first B column of the MN-major tile
+    const int nkb = (p.k + kBlockK - 1) / kBlockK;
+    const int split = gridDim.z;
+    const int kb0 = static_cast<int>(blockIdx.z) * nkb / split;
+    const int kb1 = (static_cast<int>(blockIdx.z) + 1) * nkb / split;
+
+    // ---------------------------------------------------------- producer --
+    if (kTma) {
+        if (warp == 4 && lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
+                uint8_t* s_k = smem + stage * Cfg::kStageBytes;
+                uint8_t* s_mn = s_k + Cfg::kKBytes;
+                const uint32_t extra = (p.inject && kb == kb0) ? 16u : 0u;
+                mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes + extra);
+                tma_load_2d(s_k, &tm_k, &full[stage], kb * kBlockK, k_rows0);
+#pragma unroll
+                for (int j = 0; j < Cfg::kMNCols / 64; ++j)
+                    tma_load_2d(s_mn + j * kChunkBytes, &tm_mn, &full[stage], mn_cols0 + 64 * j,
+                                kb * kBlockK);
+                ++issued;
+                if (++stage == kStages) { stage = 0; phase ^= 1u; }
+            }
+            if (!ok || *abort_flag) drain_tma<kStages>(full, issued);
+        }
+    } else if (warp < 4) {
+        const int tid = threadIdx.x;
+        uint32_t stage = 0, phase = 0;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) break;
+            uint8_t* s_k = smem + stage * Cfg::kStageBytes;
+            uint8_t* s_mn = s_k + Cfg::kKBytes;
+            load_kmaj_generic<Cfg::kKRows>(s_k, p.a, p.lda, p.m, p.k, k_rows0, kb * kBlockK, tid);
+            load_mnmaj_generic<Cfg::kMNCols>(s_mn, p.b, p.ldb, p.k, p.n, mn_cols0, kb * kBlockK, tid);
+            fence_async_shared();
+            mbar_arrive(&full[stage]);
+            if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+    }
+
+    // ------------------------------------------------------- MMA issuer --
+    if (warp == 5 && lane == 0) {
+        uint32_t stage = 0, phase = 0;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
+            tc_fence_after_sync();
+            const uint32_t s_k = smem_addr(smem + stage * Cfg::kStageBytes);
+            const uint32_t s_mn = s_k + Cfg::kKBytes;
+#pragma unroll
+            for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                const uint64_t dk = kmaj_desc(s_k, kk);
+                const uint64_t dmn = mnmaj_desc(s_mn, kk);
+                tc_mma_f16(tmem_base, kSwap ? dmn : dk, kSwap ? dk : dmn, Cfg::kIdesc,
+                           (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+            tc_commit(&empty[stage]);
+            if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) {
+            tc_commit(tfull);
+        } else {
+            tc_commit(drain);
+            mbar_wait_drain(drain, 0, kDrainLimitNs);
+        }
+    }
+    __syncwarp();
+
+    // --------------------------------------------------------- epilogue --
+    const bool split_k = split > 1;
+    if (warp < 4) {
+        // Warp-uniform: tcgen05.ld below is .sync.aligned.
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull, 0, wc));
+        tc_fence_after_sync();
+        if (ok) {
+            const int r = warp * 32 + lane;   // accumulator row = TMEM lane
+            const uint32_t t_row = tmem_base + ((warp * 32u) << 16);
+            float* red = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+            for (int c = 0; c < kBNm; c += Cfg::kChunk) {
+                uint32_t v[Cfg::kChunk];
+                if constexpr (Cfg::kChunk == 32) {
+                    tmem_ld_32x32b_x32(t_row + c, v);
+                } else {
+                    tmem_ld_32x32b_x16(t_row + c, v);
+                }
+                tmem_wait_ld();
+                if (split_k) {
+                    if constexpr (kSwap) {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kChunk; ++j)
+                            red[(c + j) * Cfg::kRedStride + r] = __uint_as_float(v[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kChunk; j += 4)
+                            *reinterpret_cast<float4*>(red + r * Cfg::kRedStride + c + j) =
+                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                            __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                    }
+                } else if constexpr (kSwap) {
+                    store_col_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
+                } else {
+                    store_row_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
+                }
+            }
+        }
+        tc_fence_before_sync();
+    }
+
+    if (split_k) {
+        // Every CTA of the cluster has its FP32 partial in shared memory; each
+        // reduces an equal slice of the tile over ranks 0..split-1 in order.
+        cluster_sync();
+        const uint32_t rank = cluster_ctarank();
+        constexpr uint32_t kQuadsPerRow = kSwap ? (kMmaM / 4) : (kBNm / 4);
+        constexpr uint32_t kQuads = Cfg::kRedRows * kQuadsPerRow;
+        const uint32_t q0 = rank * kQuads / split, q1 = (rank + 1) * kQuads / split;
+        const uint32_t red_base = smem_addr(smem);
+        for (uint32_t q = q0 + threadIdx.x; q < q1; q += kThreads) {
+            const uint32_t rr = q / kQuadsPerRow, cc = (q % kQuadsPerRow) * 4;
+            const uint32_t off = red_base + (rr * Cfg::kRedStride + cc) * 4u;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < split; ++s) {
+                const float4 v = ld_dsmem_f4(map_to_rank(off, s));
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            if constexpr (kSwap) {
+                store_quad(p, acc_col0 + rr, acc_row0 + cc, acc);   // row = m, cols = n
+            } else {
+                store_quad(p, acc_row0 + rr, acc_col0 + cc, acc);
+            }
+        }
+        cluster_sync();
+    }
+
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ==================================================== persistent kernel ====
+
+template <int kBN, int kStages>
+struct PersistCfg {
+    static constexpr uint32_t kABytes = kMmaM * 128u;        // 128 x 64 halves
+    static constexpr uint32_t kBBytes = kBN * 128u;          // 64 x kBN halves
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kBarBytes = 256;
+    static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
+    static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kBN);
+    static constexpr uint32_t kIdesc = make_idesc_f16(kMmaM, kBN, false, true);
+    static_assert(kBN % 64 == 0 && kBN <= 256, "tile width");
+    static_assert(2 * kStages + 5 <= 30, "barrier area");
+    static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m,
+                                            int& tm, int& tn) {
+    const int width = group_m * tiles_n;
+    const int g = t / width;
+    const int first_m = g * group_m;
+    const int gsz = min(tiles_m - first_m, group_m);
+    const int in = t - g * width;
+    tm = first_m + in % gsz;
+    tn = in / gsz;
+}
+
+template <int kBN, int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const GemmParams p) {
+    using Cfg = PersistCfg<kBN, kStages>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align_1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;      // [2]
+    uint64_t* tempty = tfull + 2;           // [2]
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_index();
+    const uint32_t lane = threadIdx.x & 31u;
+
+    if (warp == 4 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1u);
+            mbar_init(&empty[s], 1u);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1u);
+            mbar_init(&tempty[i], 128u);
+        }
+        mbar_init(drain, 1u);
+        *abort_flag = 0;
+        mbar_init_fence();
+        tma_prefetch_map(&tm_a);
+        tma_prefetch_map(&tm_b);
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+    const int tiles_m = (p.m + kMmaM - 1) / kMmaM;
+    const int tiles_n = (p.n + kBN - 1) / kBN;
+    const int num_tiles = tiles_m * tiles_n;
+    const int nkb = (p.k + kBlockK - 1) / kBlockK;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
+                    uint8_t* s_a = smem + stage * Cfg::kStageBytes;
+                    uint8_t* s_b = s_a + Cfg::kABytes;
+                    const uint32_t extra = (p.inject && issued == 0) ? 16u : 0u;
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes + extra);
+                    tma_load_2d(s_a, &tm_a, &full[stage], kb * kBlockK, tm * kMmaM);
+#pragma unroll
+                    for (int j = 0; j < kBN / 64; ++j)
+                        tma_load_2d(s_b + j * kChunkBytes, &tm_b, &full[stage], tn * kBN + 64 * j,
+                                    kb * kBlockK);
+                    ++issued;
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok || *abort_flag) drain_tma<kStages>(full, issued);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, iter = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++iter) {
+                const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, wc)) { ok = false; break; }
+                tc_fence_after_sync();
+                const uint32_t d = tmem_base + acc * kBN;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
+                    tc_fence_after_sync();
+                    const uint32_t s_a = smem_addr(smem + stage * Cfg::kStageBytes);
+                    const uint32_t s_b = s_a + Cfg::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 16; ++kk)
+                        tc_mma_f16(d, kmaj_desc(s_a, kk), mnmaj_desc(s_b, kk), Cfg::kIdesc,
+                                   (kb > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&empty[stage]);
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+            }
+            if (!ok) {
+                tc_commit(drain);
+                mbar_wait_drain(drain, 0, kDrainLimitNs);
+            }
+        }
+    } else {
+        // Epilogue warps 0-3: warp w owns TMEM lanes 32w .. 32w + 31.
+        const uint32_t t_lane = (warp * 32u) << 16;
+        uint32_t iter = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
+            const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wc))) break;
+            tc_fence_after_sync();
+            int tm, tn;
+            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+            const int row = tm * kMmaM + warp * 32 + lane;
+            const uint32_t t_acc = tmem_base + t_lane + acc * kBN;
+#pragma unroll 1
+            for (int c = 0; c < kBN; c += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(t_acc + c, v);
+                tmem_wait_ld();
+                store_row_segment<32>(p, row, tn * kBN + c, v);
+            }
+            tc_fence_before_sync();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+}  // namespace hgemm

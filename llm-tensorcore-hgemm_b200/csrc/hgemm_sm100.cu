@@ -1,0 +1,419 @@
+// C-ABI implementation of the sm_100a HGEMM library (include/hgemm_sm100.h):
+// argument checks, the `auto` shape heuristic, TMA descriptor encoding and
+// caching, and kernel launches on the caller's stream.
+//
+// Counterpart of the reference's host dispatch (csrc/dispatch.cpp:47-96) and
+// of the per-backend launchers (csrc/v6_mma_async.cu:408-486 and friends),
+// without torch types: the torch-facing checks live in the pybind11 module.
+#include "hgemm_sm100.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "hgemm_kernels.cuh"
+
+namespace {
+
+using namespace hgemm;
+
+__device__ int g_status_word;  // status word used when the caller passes none
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSplit = 16;
+constexpr uint64_t kDefaultTimeoutNs = 2000ull * 1000ull * 1000ull;
+
+const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
+    "auto",
+    "tc_persistent_128x256",
+    "tc_persistent_128x128",
+    "tc_splitk_128x128",
+    "tc_swapab",
+    "tc_generic_128x128",
+};
+
+// ------------------------------------------------------ device properties --
+
+struct DeviceInfo {
+    int sms = 0;
+    int major = 0, minor = 0;
+    int* status_word = nullptr;
+    int max_cluster = 8;
+};
+
+DeviceInfo g_devices[kMaxDevices];
+std::once_flag g_device_once[kMaxDevices];
+int g_device_error[kMaxDevices];
+
+int device_info(const DeviceInfo** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return HGEMM_SM100_ERR_CUDA;
+    std::call_once(g_device_once[dev], [dev] {
+        DeviceInfo& d = g_devices[dev];
+        int err = 0;
+        err |= cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess;
+        err |= cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess;
+        err |= cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess;
+        if (!err && d.major == 10 && d.minor == 0) {
+            err |= cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status_word), g_status_word) !=
+                   cudaSuccess;
+        }
+        g_device_error[dev] = err ? HGEMM_SM100_ERR_CUDA
+                                  : ((d.major == 10 && d.minor == 0) ? HGEMM_SM100_OK
+                                                                     : HGEMM_SM100_ERR_UNSUPPORTED_DEVICE);
+    });
+    *out = &g_devices[dev];
+    return g_device_error[dev];
+}
+
+// ------------------------------------------------------------ tensor maps --
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(p);
+    }();
+    return fn;
+}
+
+struct MapKey {
+    const void* base;
+    uint64_t inner, outer, ld;
+    uint32_t box_inner, box_outer;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && inner == o.inner && outer == o.outer && ld == o.ld &&
+               box_inner == o.box_inner && box_outer == o.box_outer;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        size_t h = reinterpret_cast<size_t>(k.base);
+        h ^= (k.inner * 0x9E3779B97F4A7C15ull) + (h << 6) + (h >> 2);
+        h ^= (k.outer * 0xC2B2AE3D27D4EB4Full) + (h << 6) + (h >> 2);
+        h ^= (k.ld * 0x165667B19E3779F9ull) + (h << 6) + (h >> 2);
+        h ^= (static_cast<size_t>(k.box_inner) << 32 | k.box_outer) + (h << 6) + (h >> 2);
+        return h;
+    }
+};
+
+// 2-D FP16 row-major matrix [outer x inner] with row pitch `ld` elements,
+// 128-byte swizzled boxes of [box_outer x box_inner]; out-of-range elements
+// read as zero. Descriptors are cached per thread (they depend only on the
+// key, so a reused address with the same shape reuses a valid descriptor).
+int tensor_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+               uint32_t box_inner, uint32_t box_outer) {
+    thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{base, inner, outer, ld, box_inner, box_outer};
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return HGEMM_SM100_OK;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return HGEMM_SM100_ERR_TENSOR_MAP;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap map;
+    const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
+                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return HGEMM_SM100_ERR_TENSOR_MAP;
+    if (cache.size() >= 256) cache.clear();
+    cache.emplace(key, map);
+    *out = map;
+    return HGEMM_SM100_OK;
+}
+
+// ---------------------------------------------------------------- kernels --
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemmParams);
+
+struct KernelEntry {
+    const void* fn;
+    uint32_t smem;
+    std::atomic<uint64_t> ready{0};  // bit d: attributes set on device d
+};
+
+template <typename Cfg>
+constexpr uint32_t smem_of() { return Cfg::kSmemBytes; }
+
+int prepare_kernel(KernelEntry& k, int dev) {
+    const uint64_t bit = 1ull << dev;
+    if (k.ready.load(std::memory_order_acquire) & bit) return HGEMM_SM100_OK;
+    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(k.smem)) != cudaSuccess)
+        return HGEMM_SM100_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+        return HGEMM_SM100_ERR_LAUNCH;
+    k.ready.fetch_or(bit, std::memory_order_acq_rel);
+    return HGEMM_SM100_OK;
+}
+
+#define HG_TILE(BN, SWAP, TMA, ST)                                                        \
+    KernelEntry {                                                                          \
+        reinterpret_cast<const void*>(&hgemm_tile_kernel<BN, SWAP, TMA, ST>),              \
+            TileCfg<BN, SWAP, TMA, ST>::kSmemBytes                                         \
+    }
+#define HG_PERSIST(BN, ST)                                                                \
+    KernelEntry {                                                                          \
+        reinterpret_cast<const void*>(&hgemm_persistent_kernel<BN, ST>),                   \
+            PersistCfg<BN, ST>::kSmemBytes                                                 \
+    }
+
+KernelEntry g_persist_256 = HG_PERSIST(256, 4);
+KernelEntry g_persist_128 = HG_PERSIST(128, 6);
+KernelEntry g_splitk_128 = HG_TILE(128, false, true, 6);
+KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
+KernelEntry g_swap_16 = HG_TILE(16, true, true, 8);
+KernelEntry g_swap_32 = HG_TILE(32, true, true, 8);
+KernelEntry g_swap_64 = HG_TILE(64, true, true, 6);
+KernelEntry g_swap_128 = HG_TILE(128, true, true, 5);
+KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
+
+struct SwapChoice {
+    int bnm;
+    KernelEntry* k;
+};
+SwapChoice swap_choice(int64_t m) {
+    if (m <= 16) return {16, &g_swap_16};
+    if (m <= 32) return {32, &g_swap_32};
+    if (m <= 64) return {64, &g_swap_64};
+    if (m <= 128) return {128, &g_swap_128};
+    return {256, &g_swap_256};
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+bool tma_eligible(const HgemmSm100Args& a) {
+    return (reinterpret_cast<uintptr_t>(a.a) % 16 == 0) && (reinterpret_cast<uintptr_t>(a.b) % 16 == 0) &&
+           (a.lda % 8 == 0) && (a.ldb % 8 == 0);
+}
+
+// K splits for a tile kernel: enough clusters to cover the SMs once, at most
+// one K block per split, at most the cluster limit.
+int choose_split(int64_t base_ctas, int64_t nkb, int sms, int max_split) {
+    int64_t s = sms / (base_ctas > 0 ? base_ctas : 1);
+    if (s < 1) s = 1;
+    if (s > max_split) s = max_split;
+    if (s > nkb) s = nkb;
+    return static_cast<int>(s);
+}
+
+int check_args(const HgemmSm100Args* a) {
+    if (a == nullptr || a->a == nullptr || a->b == nullptr || a->c == nullptr)
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (a->m <= 0 || a->n <= 0 || a->k <= 0) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    const int64_t lim = (int64_t{1} << 31) - 1;
+    if (a->m > lim || a->n > lim || a->k > lim) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (a->lda < a->k || a->ldb < a->n || a->ldc < a->n) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (a->config < 0 || a->config >= HGEMM_SM100_CFG_COUNT) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    if (a->split_k < 0 || a->split_k > kMaxSplit) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    return HGEMM_SM100_OK;
+}
+
+int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, int32_t* split_out) {
+    int32_t cfg = a.config;
+    const int64_t nkb = cdiv(a.k, kBlockK);
+    const int sms = dev.sms > 0 ? dev.sms : 148;
+    if (!tma_eligible(a)) {
+        cfg = HGEMM_SM100_CFG_GENERIC_128x128;
+    } else if (cfg == HGEMM_SM100_CFG_AUTO) {
+        const int64_t tiles_256 = cdiv(a.m, 128) * cdiv(a.n, 256);
+        const int64_t tiles_128 = cdiv(a.m, 128) * cdiv(a.n, 128);
+        if (a.m <= 256) cfg = HGEMM_SM100_CFG_SWAPAB;
+        else if (tiles_256 >= 2 * sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x256;
+        else if (tiles_128 >= sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x128;
+        else cfg = HGEMM_SM100_CFG_SPLITK_128x128;
+    }
+    if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x128;
+
+    int32_t split = 1;
+    if (cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_GENERIC_128x128 ||
+        cfg == HGEMM_SM100_CFG_SWAPAB) {
+        int64_t base;
+        if (cfg == HGEMM_SM100_CFG_SWAPAB) base = cdiv(a.n, 128) * cdiv(a.m, swap_choice(a.m).bnm);
+        else base = cdiv(a.m, 128) * cdiv(a.n, 128);
+        split = a.split_k > 0 ? a.split_k : choose_split(base, nkb, sms, dev.max_cluster);
+        if (split > nkb) split = static_cast<int32_t>(nkb);
+        if (split < 1) split = 1;
+    }
+    *cfg_out = cfg;
+    *split_out = split;
+    return HGEMM_SM100_OK;
+}
+
+int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0, const CUtensorMap& m1,
+           const GemmParams& p, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = k.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (cluster_z > 1) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    const KernelFn fn = reinterpret_cast<KernelFn>(const_cast<void*>(k.fn));
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, m0, m1, p);
+    return e == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
+}
+
+}  // namespace
+
+// ================================================================== C ABI ==
+
+extern "C" int hgemm_sm100_resolve(const HgemmSm100Args* args, int32_t* config_out, int32_t* split_out) {
+    int rc = check_args(args);
+    if (rc != HGEMM_SM100_OK) return rc;
+    if (config_out == nullptr || split_out == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    const DeviceInfo* dev = nullptr;
+    rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    return resolve(*args, *dev, config_out, split_out);
+}
+
+extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
+    int rc = check_args(args);
+    if (rc != HGEMM_SM100_OK) return rc;
+    const DeviceInfo* dev = nullptr;
+    rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    int devid = 0;
+    cudaGetDevice(&devid);
+    const HgemmSm100Args& a = *args;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+
+    int32_t cfg = 0, split = 1;
+    rc = resolve(a, *dev, &cfg, &split);
+    if (rc != HGEMM_SM100_OK) return rc;
+
+    GemmParams p{};
+    p.a = static_cast<const __half*>(a.a);
+    p.b = static_cast<const __half*>(a.b);
+    p.c = a.c;
+    p.m = static_cast<int>(a.m);
+    p.n = static_cast<int>(a.n);
+    p.k = static_cast<int>(a.k);
+    p.lda = a.lda;
+    p.ldb = a.ldb;
+    p.ldc = a.ldc;
+    p.out_f32 = (a.flags & HGEMM_SM100_FLAG_OUT_F32) ? 1 : 0;
+    const uintptr_t c_align = p.out_f32 ? 16 : 16;
+    p.vec_ok = (reinterpret_cast<uintptr_t>(a.c) % c_align == 0) && (a.ldc % 8 == 0);
+    p.group_m = 16;
+    p.inject = (a.flags & HGEMM_SM100_FLAG_TEST_INJECT_TX) ? 1 : 0;
+    p.status = a.status != nullptr ? a.status : dev->status_word;
+    p.timeout_ns = a.timeout_ns != 0 ? a.timeout_ns : kDefaultTimeoutNs;
+
+    CUtensorMap map_k, map_mn;
+    std::memset(&map_k, 0, sizeof(map_k));
+    std::memset(&map_mn, 0, sizeof(map_mn));
+    const uint64_t M = a.m, N = a.n, K = a.k;
+
+    switch (cfg) {
+        case HGEMM_SM100_CFG_PERSISTENT_128x256:
+        case HGEMM_SM100_CFG_PERSISTENT_128x128: {
+            const bool wide = cfg == HGEMM_SM100_CFG_PERSISTENT_128x256;
+            KernelEntry& k = wide ? g_persist_256 : g_persist_128;
+            const int bn = wide ? 256 : 128;
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
+            const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, bn);
+            const int64_t grid = tiles < dev->sms ? tiles : dev->sms;
+            return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_SPLITK_128x128: {
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(g_splitk_128, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
+                            static_cast<unsigned>(split));
+            return launch(g_splitk_128, grid, split, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_SWAPAB: {
+            const SwapChoice sc = swap_choice(a.m);
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(sc.bnm))) !=
+                HGEMM_SM100_OK)
+                return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(*sc.k, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
+                            static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
+            return launch(*sc.k, grid, split, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_GENERIC_128x128: {
+            if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
+                            static_cast<unsigned>(split));
+            return launch(g_generic_128, grid, split, map_k, map_mn, p, stream);
+        }
+        default:
+            return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    }
+}
+
+extern "C" int32_t hgemm_sm100_config_from_name(const char* name) {
+    if (name == nullptr) return -1;
+    for (int32_t i = 0; i < HGEMM_SM100_CFG_COUNT; ++i)
+        if (std::strcmp(name, kConfigNames[i]) == 0) return i;
+    return -1;
+}
+
+extern "C" const char* hgemm_sm100_config_name(int32_t config) {
+    if (config < 0 || config >= HGEMM_SM100_CFG_COUNT) return nullptr;
+    return kConfigNames[config];
+}
+
+extern "C" int32_t hgemm_sm100_num_configs(void) { return HGEMM_SM100_CFG_COUNT; }
+
+extern "C" size_t hgemm_sm100_workspace_bytes(int32_t, int64_t, int64_t, int64_t) { return 0; }
+
+extern "C" const char* hgemm_sm100_status_string(int status) {
+    switch (status) {
+        case HGEMM_SM100_OK: return "ok";
+        case HGEMM_SM100_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case HGEMM_SM100_ERR_UNKNOWN_CONFIG: return "unknown implementation";
+        case HGEMM_SM100_ERR_UNSUPPORTED_DEVICE: return "device is not an sm_100 (B200) GPU";
+        case HGEMM_SM100_ERR_LAUNCH: return "kernel launch failed";
+        case HGEMM_SM100_ERR_PIPELINE_TIMEOUT: return "hgemm: pipeline timeout";
+        case HGEMM_SM100_ERR_TENSOR_MAP: return "TMA descriptor encoding failed";
+        case HGEMM_SM100_ERR_CUDA: return "CUDA runtime error";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int hgemm_sm100_read_status(int32_t* value, int clear) {
+    if (value == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    const DeviceInfo* dev = nullptr;
+    int rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    if (cudaDeviceSynchronize() != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpy(&v, dev->status_word, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return HGEMM_SM100_ERR_CUDA;
+    *value = v;
+    if (clear && cudaMemset(dev->status_word, 0, sizeof(int)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    return HGEMM_SM100_OK;
+}

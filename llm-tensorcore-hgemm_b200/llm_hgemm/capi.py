@@ -1,0 +1,111 @@
+"""ctypes binding of the C ABI in include/hgemm_sm100.h.
+
+This is the binding a non-torch host (or any FFI user) writes against
+``libhgemm_sm100.so``; the tests use it to call the kernels through the C
+boundary directly. ``load()`` only opens the library (no GPU needed).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libhgemm_sm100.so"
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_UNKNOWN_CONFIG = 2
+ERR_UNSUPPORTED_DEVICE = 3
+ERR_LAUNCH = 4
+ERR_PIPELINE_TIMEOUT = 5
+ERR_TENSOR_MAP = 6
+ERR_CUDA = 7
+
+CFG_AUTO = 0
+CFG_PERSISTENT_128x256 = 1
+CFG_PERSISTENT_128x128 = 2
+CFG_SPLITK_128x128 = 3
+CFG_SWAPAB = 4
+CFG_GENERIC_128x128 = 5
+
+FLAG_OUT_F32 = 1
+FLAG_TEST_INJECT_TX = 2
+
+
+class HgemmSm100Args(ctypes.Structure):
+    _fields_ = [
+        ("a", ctypes.c_void_p),
+        ("b", ctypes.c_void_p),
+        ("c", ctypes.c_void_p),
+        ("m", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("lda", ctypes.c_int64),
+        ("ldb", ctypes.c_int64),
+        ("ldc", ctypes.c_int64),
+        ("config", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("timeout_ns", ctypes.c_uint64),
+    ]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(str(LIB_PATH))
+        lib.hgemm_sm100_run.argtypes = [ctypes.POINTER(HgemmSm100Args), ctypes.c_void_p]
+        lib.hgemm_sm100_run.restype = ctypes.c_int
+        lib.hgemm_sm100_resolve.argtypes = [ctypes.POINTER(HgemmSm100Args),
+                                            ctypes.POINTER(ctypes.c_int32),
+                                            ctypes.POINTER(ctypes.c_int32)]
+        lib.hgemm_sm100_resolve.restype = ctypes.c_int
+        lib.hgemm_sm100_config_from_name.argtypes = [ctypes.c_char_p]
+        lib.hgemm_sm100_config_from_name.restype = ctypes.c_int32
+        lib.hgemm_sm100_config_name.argtypes = [ctypes.c_int32]
+        lib.hgemm_sm100_config_name.restype = ctypes.c_char_p
+        lib.hgemm_sm100_num_configs.argtypes = []
+        lib.hgemm_sm100_num_configs.restype = ctypes.c_int32
+        lib.hgemm_sm100_workspace_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64,
+                                                    ctypes.c_int64, ctypes.c_int64]
+        lib.hgemm_sm100_workspace_bytes.restype = ctypes.c_size_t
+        lib.hgemm_sm100_status_string.argtypes = [ctypes.c_int]
+        lib.hgemm_sm100_status_string.restype = ctypes.c_char_p
+        lib.hgemm_sm100_read_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int]
+        lib.hgemm_sm100_read_status.restype = ctypes.c_int
+        _lib = lib
+    return _lib
+
+
+def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
+              lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
+              config: int = CFG_AUTO, split_k: int = 0, flags: int = 0,
+              status_ptr: int | None = None, timeout_ns: int = 0) -> HgemmSm100Args:
+    return HgemmSm100Args(a_ptr, b_ptr, c_ptr, m, n, k,
+                          k if lda is None else lda, n if ldb is None else ldb,
+                          n if ldc is None else ldc, config, split_k, flags,
+                          status_ptr, timeout_ns)
+
+
+def run(args: HgemmSm100Args, stream: int = 0) -> int:
+    return load().hgemm_sm100_run(ctypes.byref(args), ctypes.c_void_p(stream))
+
+
+def resolve(args: HgemmSm100Args) -> tuple[int, int, int]:
+    cfg, split = ctypes.c_int32(0), ctypes.c_int32(0)
+    rc = load().hgemm_sm100_resolve(ctypes.byref(args), ctypes.byref(cfg), ctypes.byref(split))
+    return rc, cfg.value, split.value
+
+
+def status_string(code: int) -> str:
+    return load().hgemm_sm100_status_string(code).decode()
+
+
+def read_status(clear: bool = True) -> tuple[int, int]:
+    v = ctypes.c_int32(0)
+    rc = load().hgemm_sm100_read_status(ctypes.byref(v), 1 if clear else 0)
+    return rc, v.value

@@ -1,0 +1,148 @@
+"""Pipeline edge cases: exact stage-marker known answers for every ring
+depth, explicit K splits, guard bands around the output, NaN-prefilled
+outputs on a side stream, misaligned operands.
+
+Counterparts of reference tests/test_v6_async.py:21-99 and
+tests/test_v5_vectorized.py:40-76."""
+
+import pytest
+import torch
+
+from llm_hgemm import capi, hgemm
+from llm_hgemm.ops import _hgemm_out, backend_info
+from oracle import reference as oracle
+from tests.gpu_helpers import IMPLEMENTATIONS, assert_gate, require_cuda, seeded_inputs
+
+pytestmark = pytest.mark.gpu
+
+CONFIG_IDS = {
+    "tc_persistent_128x256": capi.CFG_PERSISTENT_128x256,
+    "tc_persistent_128x128": capi.CFG_PERSISTENT_128x128,
+    "tc_splitk_128x128": capi.CFG_SPLITK_128x128,
+    "tc_swapab": capi.CFG_SWAPAB,
+    "tc_generic_128x128": capi.CFG_GENERIC_128x128,
+}
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _cuda():
+    require_cuda()
+
+
+def run_capi(a, b, out, config, split_k=0, flags=0):
+    m, k = a.shape
+    n = b.shape[1]
+    args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
+                          config=config, split_k=split_k, flags=flags)
+    rc = capi.run(args, torch.cuda.current_stream().cuda_stream)
+    assert rc == capi.OK, capi.status_string(rc)
+    return out
+
+
+@pytest.mark.parametrize("impl", IMPLEMENTATIONS)
+def test_reference_stage_markers(impl):
+    """Reference tests/test_v6_async.py:88-99 verbatim: exactly 7.75."""
+    m, n, k = 129, 136, 160
+    a, b, value = oracle.stage_marker_inputs(m, n, k, 32, device="cuda")
+    out = hgemm(a, b, implementation=impl)
+    torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("impl", IMPLEMENTATIONS)
+@pytest.mark.parametrize("kblocks", [1, 2, 3, 4, 5, 6, 7, 9, 13])
+@pytest.mark.parametrize("mn", [(129, 136), (8, 300), (256, 512)])
+def test_stage_markers_every_ring_depth(impl, kblocks, mn):
+    m, n = mn
+    a, b, value = oracle.stage_marker_inputs(m, n, 64 * kblocks, 64, device="cuda")
+    out = hgemm(a, b, implementation=impl)
+    torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("config", ["tc_splitk_128x128", "tc_swapab", "tc_generic_128x128"])
+@pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 8, 16])
+def test_explicit_split_k(config, split):
+    m, n, k = (48, 384, 64 * 17) if config == "tc_swapab" else (200, 260, 64 * 17)
+    a, b, value = oracle.stage_marker_inputs(m, n, k, 64, device="cuda")
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    run_capi(a, b, out, CONFIG_IDS[config], split_k=split)
+    torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
+    a, b = seeded_inputs(m, n, k + 5)
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    run_capi(a, b, out, CONFIG_IDS[config], split_k=split)
+    assert_gate(out, a, b)
+
+
+@pytest.mark.parametrize("config", list(CONFIG_IDS))
+@pytest.mark.parametrize("shape", [(127, 129, 63), (200, 264, 520), (3, 1000, 300)])
+def test_guard_bands_untouched(config, shape):
+    m, n, k = shape
+    a, b = seeded_inputs(m, n, k)
+    pad = 4096
+    buf = torch.full((pad + m * n + pad,), 1234.0, device="cuda", dtype=torch.float16)
+    out = buf[pad:pad + m * n].view(m, n)
+    run_capi(a, b, out, CONFIG_IDS[config])
+    torch.cuda.synchronize()
+    assert torch.all(buf[:pad] == 1234.0) and torch.all(buf[pad + m * n:] == 1234.0)
+    assert_gate(out, a, b)
+
+
+@pytest.mark.parametrize("impl", IMPLEMENTATIONS)
+@pytest.mark.parametrize("shape", [(128, 128, 96), (127, 136, 40), (127, 129, 63)])
+def test_non_default_stream_preallocated_nan(impl, shape):
+    a, b = seeded_inputs(*shape)
+    reference = oracle.torch_reference(a.cpu(), b.cpu())
+    out = torch.full(shape[:2], float("nan"), device="cuda", dtype=torch.float16)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        returned = _hgemm_out(a, b, out, implementation=impl)
+    torch.cuda.current_stream().wait_stream(stream)
+    assert returned is out
+    metrics = oracle.error_metrics(out.cpu(), reference)
+    assert oracle.correctness_passed(metrics), metrics
+
+
+@pytest.mark.parametrize("impl", IMPLEMENTATIONS)
+@pytest.mark.parametrize("offset_a,offset_b", [(1, 0), (0, 1), (1, 1)])
+def test_misaligned_storage(impl, offset_a, offset_b):
+    torch.manual_seed(2026)
+    m, n, k = 128, 128, 64
+    a_storage = torch.randn(m * k + offset_a, device="cuda", dtype=torch.float16) * 0.1
+    b_storage = torch.randn(k * n + offset_b, device="cuda", dtype=torch.float16) * 0.1
+    a = a_storage[offset_a:].view(m, k)
+    b = b_storage[offset_b:].view(k, n)
+    assert a.data_ptr() % 16 == offset_a * 2 and b.data_ptr() % 16 == offset_b * 2
+    assert_gate(hgemm(a, b, implementation=impl), a, b)
+
+
+@pytest.mark.parametrize("config", list(CONFIG_IDS))
+def test_misaligned_output(config):
+    m, n, k = 70, 136, 72
+    a, b = seeded_inputs(m, n, k)
+    storage = torch.full((m * n + 1,), float("nan"), device="cuda", dtype=torch.float16)
+    out = storage[1:].view(m, n)
+    run_capi(a, b, out, CONFIG_IDS[config])
+    assert_gate(out, a, b)
+
+
+@pytest.mark.parametrize("impl", IMPLEMENTATIONS)
+def test_provider_metadata(impl):
+    assert backend_info(impl) == {"algorithm_id": -1, "workspace_bytes": 0}
+
+
+@pytest.mark.parametrize("config", list(CONFIG_IDS))
+def test_fp32_output(config):
+    m, n, k = 100, 264, 1000
+    a, b = seeded_inputs(m, n, k)
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
+    run_capi(a, b, out, CONFIG_IDS[config], flags=capi.FLAG_OUT_F32)
+    ref = torch.mm(a.cpu().float(), b.cpu().float())
+    torch.testing.assert_close(out.cpu(), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_capi_matches_module_bitwise():
+    a, b = seeded_inputs(300, 520, 1000)
+    for name, cfg in CONFIG_IDS.items():
+        out = torch.empty((300, 520), device="cuda", dtype=torch.float16)
+        run_capi(a, b, out, cfg)
+        assert torch.equal(out, hgemm(a, b, implementation=name)), name
