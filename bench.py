@@ -1,0 +1,545 @@
+"""Benchmark of the B200 FP16 HGEMM hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workloads:
+  * N = 1: ``square_8192`` - C[8192,8192] = A[8192,8192] @ B[8192,8192], FP16
+    in, FP32 accumulate, FP16 out; one step = one ``hgemm`` launch on inputs
+    already resident in HBM (256 MiB of inputs > the 126 MB L2, so no flush is
+    needed between steps). ``value`` is TFLOP/s = 2*M*N*K / step time.
+    A per-shape ``sweep`` (square sizes, ragged sizes, Qwen3-4B linear shapes)
+    reports each shape's median launch time, TFLOP/s, % of measured peak and
+    the ratio to cuBLASLt measured in the same process.
+  * N > 1 (torchrun, one rank per GPU, NCCL): ``tp_mlp`` - the tensor-parallel
+    MLP of configs[4]: up-proj X[8192,8192] @ W_up[8192,28672] split on N (no
+    communication), down-proj H[8192,28672] @ W_down[28672,8192] split on K
+    with FP32 partials all-reduced over NVLink and rounded to FP16 once.
+    ``value`` is the whole-job TFLOP/s of both GEMMs over the max-over-ranks
+    step time (strong scaling: the total work is fixed).
+
+``--impl reference`` times the reference's CPU path (its oracle: FP32 matmul
+of the FP16 operands, rounded to FP16, oracle/reference.py) on the host cores,
+on bounded row samples of the same workload; under torchrun only rank 0 runs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+PKG = REPO / "llm-tensorcore-hgemm_b200"
+for _p in (str(REPO), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "FP16 TFLOPS (% of B200 peak) per shape; Qwen3-4B linear-layer µs vs cuBLASLt"
+UNIT = "TFLOP/s"
+SEED = 2026
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+QWEN_LAYERS = {  # (K, N) of the Qwen3-4B linears, weights stored [K, N]
+    "q_proj": (2560, 4096), "k_proj": (2560, 1024), "o_proj": (4096, 2560),
+    "gate_proj": (2560, 9728), "down_proj": (9728, 2560), "lm_head": (2560, 151936),
+}
+QWEN_M = (1, 8, 16, 64, 128, 512, 2048, 8192)
+SQUARE = (1024, 2048, 4096, 8192, 16384)
+RAGGED = ((8193, 8193, 8192), (8199, 8199, 8192), (8255, 8255, 8192), (4096, 4096, 4103),
+          (2049, 2049, 2049))
+
+
+# ------------------------------------------------------------------ utils --
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
+
+
+def load_peaks() -> tuple[dict, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text()), "measured"
+        except (OSError, ValueError):
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic() -> dict:
+    path = REPO / "profiles" / "traffic.json"
+    if path.exists():
+        try:
+            return json.loads(path.read_text())
+        except (OSError, ValueError):
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML while the
+    timed region runs (read-only queries)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.period = period_s
+        self.samples: list[tuple[int, int, float]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # NVML absent: report no samples
+            log(f"clock sampler unavailable: {exc}")
+            self._nvml = None
+
+    def _run(self) -> None:
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                power = nv.nvmlDeviceGetPowerUsage(self._handle) / 1000.0
+                self.samples.append((sm, reasons, power))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mask = 0
+        for _, r, _ in self.samples:
+            mask |= r
+        names = sorted({n for bit, n in self.REASONS.items() if mask & bit} - {"gpu_idle"})
+        return {
+            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "power_w_max": round(max(p for _, _, p in self.samples), 1),
+            "samples": len(self.samples),
+        }
+
+
+def device_time_ms(fn, steps: int, warmup: int, stream, barrier=None) -> float:
+    """Milliseconds for `steps` calls of fn, CUDA events on `stream`."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    if barrier is not None:
+        barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        fn()
+    stop.record(stream)
+    stop.synchronize()
+    torch.cuda.synchronize()
+    if barrier is not None:
+        barrier()
+    return start.elapsed_time(stop)
+
+
+# ------------------------------------------------------------ CPU baseline --
+
+def cpu_baseline(m: int, n: int, k: int, budget_s: float = 12.0) -> dict:
+    """Oracle FP32 GEMM (reference torch_reference) on host cores over row
+    samples of A; returns TFLOP/s of the sampled work."""
+    from oracle import reference as oracle
+
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(SEED)
+    b = (torch.randn((k, n), generator=g) * 0.1).half()
+    rows = min(m, 64)
+    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+    t0 = time.perf_counter()
+    oracle.torch_reference(a, b)
+    first = time.perf_counter() - t0
+    # Grow the row sample to fill about budget_s / 3 per call, 3 calls.
+    target = budget_s / 3.0
+    rows = int(min(m, max(rows, rows * target / max(first, 1e-3))))
+    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.torch_reference(a, b)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {
+        "value": round(2.0 * rows * n * k / t / 1e12, 4),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"A rows 0..{rows - 1} of the {m}x{n}x{k} problem (full N, K), "
+                  f"median of 3 calls of the oracle (FP32 matmul + FP16 rounding), "
+                  f"{threads} threads of {os.cpu_count()} CPUs",
+        "seconds_per_call": round(t, 3),
+    }
+
+
+# ----------------------------------------------------------- square / sweep --
+
+def make_sets(m: int, n: int, k: int, device, nsets: int | None = None, seed: int = SEED):
+    """Enough (A, B, C) sets that cycling through them touches more than L2."""
+    per = 2 * (m * k + k * n + m * n)
+    if nsets is None:
+        nsets = max(1, math.ceil(2 * L2_BYTES / per))
+        nsets = min(nsets, 64)
+    g = torch.Generator(device=device).manual_seed(seed)
+    a0 = (torch.randn((m, k), generator=g, device=device, dtype=torch.float32) * 0.1).half()
+    b0 = (torch.randn((k, n), generator=g, device=device, dtype=torch.float32) * 0.1).half()
+    sets = []
+    for i in range(nsets):
+        a = a0 if i == 0 else a0.clone()
+        b = b0 if i == 0 else b0.clone()
+        sets.append((a, b, torch.empty((m, n), device=device, dtype=torch.float16)))
+    return sets
+
+
+def median_launch_us(fn_for_set, sets, warmup=20, samples=50, per_sample=10) -> dict:
+    """Reference protocol (docs/benchmark_protocol.md: 20 warm-up, 50 samples of
+    10 launches, CUDA events on the current stream), rotating input sets."""
+    stream = torch.cuda.current_stream()
+    idx = 0
+    for _ in range(warmup):
+        fn_for_set(sets[idx % len(sets)])
+        idx += 1
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(samples):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        for _ in range(per_sample):
+            fn_for_set(sets[idx % len(sets)])
+            idx += 1
+        e.record(stream)
+        e.synchronize()
+        out.append(s.elapsed_time(e) * 1000.0 / per_sample)
+    out.sort()
+    return {"median_us": statistics.median(out), "p95_us": out[int(0.95 * (len(out) - 1))],
+            "min_us": out[0]}
+
+
+def gpu_reference_check(out, a, b) -> bool:
+    from oracle import reference as oracle
+
+    if a.shape[0] * b.shape[1] * a.shape[1] <= 2048 ** 3:
+        return oracle.check(out, a, b)["passed"]
+    ref = oracle.torch_reference(a, b)  # GPU FP32 with TF32 off (reference bench_square.py:193)
+    return oracle.correctness_passed(oracle.error_metrics(out, ref))
+
+
+def sweep(peaks: dict, quick: bool) -> list[dict]:
+    import llm_hgemm
+    from llm_hgemm import _comparators
+    from llm_hgemm.ops import _hgemm_out, resolved_config
+
+    shapes = [(s, s, s, "square") for s in SQUARE]
+    shapes += [(m, n, k, "ragged") for (m, n, k) in RAGGED]
+    for layer, (k, n) in QWEN_LAYERS.items():
+        for m in QWEN_M:
+            shapes.append((m, n, k, f"qwen3_4b.{layer}"))
+    if quick:
+        shapes = [s for s in shapes if s[0] * s[1] * s[2] <= 4096 ** 3]
+    peak_t = peaks["bf16_tflops"]
+    peak_bw = peaks["hbm_gbs"]
+    rows = []
+    for (m, n, k, tag) in shapes:
+        sets = make_sets(m, n, k, "cuda")
+        ours = median_launch_us(
+            lambda s: _hgemm_out(s[0], s[1], s[2], implementation="auto"), sets)
+        lt = median_launch_us(lambda s: _comparators.cublaslt_out(s[0], s[1], s[2]), sets)
+        a, b, c = sets[0]
+        _hgemm_out(a, b, c, implementation="auto")
+        ok = gpu_reference_check(c, a, b)
+        cfg, split = resolved_config(a, b, "auto")
+        flops = 2.0 * m * n * k
+        bytes_ = 2.0 * (m * k + k * n + m * n)
+        t = ours["median_us"]
+        compute_bound = flops / bytes_ > peak_t * 1e12 / (peak_bw * 1e9)
+        rows.append({
+            "shape": f"{m}x{n}x{k}", "tag": tag, "config": cfg, "split_k": split,
+            "median_us": round(t, 2), "p95_us": round(ours["p95_us"], 2),
+            "tflops": round(flops / t / 1e6, 1),
+            "pct_of_peak": round(100.0 * flops / t / 1e6 / peak_t, 1),
+            "hbm_gbs": round(bytes_ / t / 1e3, 1),
+            "bound": "tensor" if compute_bound else "hbm",
+            "roofline_frac": round((flops / t / 1e6 / peak_t) if compute_bound
+                                   else (bytes_ / t / 1e3 / peak_bw), 3),
+            "cublaslt_us": round(lt["median_us"], 2),
+            "ratio_to_cublaslt": round(lt["median_us"] / t, 3),
+            "status": "pass" if ok else "fail",
+        })
+        log(json.dumps(rows[-1]))
+        del sets
+        torch.cuda.empty_cache()
+    return rows
+
+
+def run_square(args, peaks, peak_kind) -> dict:
+    import llm_hgemm
+    from llm_hgemm import _comparators
+    from llm_hgemm.ops import _hgemm_out, resolved_config
+
+    m = n = k = args.size
+    flops = 2.0 * m * n * k
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(SEED)
+    a = (torch.randn((m, k), generator=g, device=dev, dtype=torch.float32) * 0.1).half()
+    b = (torch.randn((k, n), generator=g, device=dev, dtype=torch.float32) * 0.1).half()
+    c = torch.empty((m, n), device=dev, dtype=torch.float16)
+    cfg, split = resolved_config(a, b, args.implementation)
+    stream = torch.cuda.current_stream()
+
+    def step():
+        _hgemm_out(a, b, c, implementation=args.implementation)
+
+    sampler = ClockSampler(dev.index)
+    with sampler:
+        ms = device_time_ms(step, args.steps, args.warmup, stream)
+    clocks = sampler.summary()
+    ms_per_step = ms / args.steps
+    value = flops / (ms_per_step * 1e-3) / 1e12
+
+    ok = gpu_reference_check(c, a, b)
+
+    # cuBLASLt on the same inputs, same protocol.
+    ref_out = torch.empty_like(c)
+    lt_ms = device_time_ms(lambda: _comparators.cublaslt_out(a, b, ref_out), args.steps,
+                           args.warmup, stream) / args.steps
+
+    # End to end through the public API with pinned host buffers: H2D of A and
+    # B, the GEMM, D2H of C, every step.
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = torch.empty((m, n), dtype=torch.float16).pin_memory()
+    a_d = torch.empty_like(a)
+    b_d = torch.empty_like(b)
+    c_d = torch.empty_like(c)
+
+    def e2e_step():
+        a_d.copy_(a_h, non_blocking=True)
+        b_d.copy_(b_h, non_blocking=True)
+        _hgemm_out(a_d, b_d, c_d, implementation=args.implementation)
+        c_h.copy_(c_d, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    e2e_ms = device_time_ms(e2e_step, e2e_steps, 2, stream) / e2e_steps
+    e2e_ok = torch.equal(c_h, c.cpu())
+
+    traffic = load_traffic().get(f"{cfg}:{m}x{n}x{k}")
+    peak = peaks["bf16_tflops"]
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": f"synthetic: randn*0.1 FP16, torch.manual_seed({SEED}) generator on device",
+        "config": {"workload": f"square_{m}", "M": m, "N": n, "K": k,
+                   "implementation": args.implementation, "kernel_config": cfg, "split_k": split,
+                   "l2": "inputs 2*(M*K+K*N) bytes exceed the 126 MB L2; no flush",
+                   "parallelism": "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(value / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)"
+                     if peak_kind == "measured" else "fallback 1.59 PFLOP/s burst",
+                     "kernel": cfg},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 1), "unit": UNIT,
+                "h2d_bytes_per_step": a.numel() * 2 + b.numel() * 2,
+                "d2h_bytes_per_step": c.numel() * 2, "ms_per_step": round(e2e_ms, 3),
+                "api": "llm_hgemm.ops._hgemm_out with pinned-host copies in the timed region",
+                "matches_device_result": bool(e2e_ok)},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "correctness": "pass" if ok else "fail",
+        "comparators": {"cublaslt_ms": round(lt_ms, 4),
+                        "cublaslt_tflops": round(flops / (lt_ms * 1e-3) / 1e12, 1),
+                        "ratio_to_cublaslt": round(lt_ms / ms_per_step, 3)},
+    }
+    del a_h, b_h, c_h, a_d, b_d, c_d, ref_out
+    return line
+
+
+# ----------------------------------------------------------------- TP MLP --
+
+def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict | None:
+    import torch.distributed as dist
+
+    from llm_hgemm.tensor_parallel import TensorParallelMLP
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    mlp = TensorParallelMLP.synthetic(rank, world, seed=SEED, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        dist.barrier(device_ids=[dev.index])
+
+    sampler = ClockSampler(dev.index)
+    with sampler:
+        ms = device_time_ms(mlp.step, args.steps, args.warmup, stream, barrier)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item()) / args.steps
+    gemm_ms = mlp.time_gemms(max(3, args.steps // 2), 2)
+    tg = torch.tensor([gemm_ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(tg, op=dist.ReduceOp.MAX)
+    gemm_ms = float(tg.item())
+    ok = mlp.check()
+    okt = torch.tensor([1 if ok else 0], device=dev)
+    dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+    if rank != 0:
+        return None
+    flops = mlp.total_flops()
+    value = flops / (ms_max * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    per_rank_gemm_tflops = flops / world / (gemm_ms * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+        "data": f"synthetic: X,H randn*0.1, W randn*0.02 FP16, seed {SEED} on every rank",
+        "config": {"workload": "tp_mlp", "up": "8192x28672x8192 (N split)",
+                   "down": "8192x8192x28672 (K split, FP32 all-reduce)",
+                   "parallelism": f"tp{world}", "l2": "operands exceed L2"},
+        "roofline": {"bound": "tensor", "achieved": round(per_rank_gemm_tflops, 1),
+                     "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(per_rank_gemm_tflops / peak, 4), "traffic": None,
+                     "aggregate_frac": round(value / (world * peak), 4),
+                     "peak_source": f"{peak_kind} bf16 burst"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": sampler.summary(),
+        "correctness": "pass" if int(okt.item()) else "fail",
+        "breakdown_ms": {"gemms": round(gemm_ms, 4), "step": round(ms_max, 4)},
+    }
+
+
+# ------------------------------------------------------ reference CPU arm --
+
+def run_reference_arm(args, workload: tuple[int, int, int], world: int) -> dict:
+    from oracle import reference as oracle
+
+    m, n, k = workload
+    threads = torch.get_num_threads()
+    g = torch.Generator().manual_seed(SEED)
+    b = (torch.randn((k, n), generator=g) * 0.1).half()
+    rows = 64
+    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+    t0 = time.perf_counter()
+    oracle.torch_reference(a, b)
+    probe = time.perf_counter() - t0
+    # Size each step to ~2 s of CPU work, whatever K and W are.
+    rows = int(min(m, max(rows, rows * 2.0 / max(probe, 1e-3))))
+    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+    for _ in range(args.warmup):
+        oracle.torch_reference(a, b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.torch_reference(a, b)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = 2.0 * rows * n * k / dt / 1e12
+    sample = (f"A rows 0..{rows - 1} of {m}x{n}x{k} per step (full N, K), "
+              f"oracle FP32 matmul + FP16 rounding, {threads} threads")
+    return {
+        "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "data": f"synthetic: randn*0.1 FP16, seed {SEED}", "impl": "reference",
+        "config": {"workload": f"square_{m}" if world == 1 else "tp_mlp", "M": m, "N": n, "K": k},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ------------------------------------------------------------------- main --
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description="HGEMM benchmark (one JSON line)")
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--implementation", default="auto", help="llm_hgemm implementation name")
+    parser.add_argument("--size", type=int, default=8192, help="square workload size (N=1)")
+    parser.add_argument("--no-sweep", action="store_true", help="skip the per-shape sweep")
+    parser.add_argument("--quick-sweep", action="store_true", help="sweep shapes <= 4096^3 only")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        workload = (args.size,) * 3 if world == 1 else (8192, 8192, 28672)
+        print(json.dumps(run_reference_arm(args, workload, world)), flush=True)
+        return
+
+    peaks, peak_kind = load_peaks()
+    if world == 1:
+        line = run_square(args, peaks, peak_kind)
+        if not args.no_sweep:
+            line["sweep"] = sweep(peaks, args.quick_sweep)
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.size, args.size, args.size)
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    try:
+        line = run_tp_mlp(args, rank, world, peaks, peak_kind)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

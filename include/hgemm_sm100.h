@@ -54,7 +54,9 @@ enum {
     HGEMM_SM100_CFG_SPLITK_128x128 = 3,    /* "tc_splitk_128x128": cluster split-K */
     HGEMM_SM100_CFG_SWAPAB = 4,            /* "tc_swapab": C^T = B^T A^T, M <= 256 */
     HGEMM_SM100_CFG_GENERIC_128x128 = 5,   /* "tc_generic_128x128": no TMA       */
-    HGEMM_SM100_CFG_COUNT = 6
+    HGEMM_SM100_CFG_PAIR_256x256 = 6,      /* "tc_pair_256x256": CTA pair,
+                                              cta_group::2, persistent          */
+    HGEMM_SM100_CFG_COUNT = 7
 };
 
 /* Flags. */

@@ -575,4 +575,182 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
     }
 }
 
+// ============================================== CTA-pair persistent kernel ====
+//
+// 256 x 256 output tiles per cluster of two CTAs (cta_group::2). CTA r of the
+// pair TMA-loads rows 128r .. 128r+127 of the A tile and columns 128r ..
+// 128r+127 of the B tile into its own shared memory; the even CTA's single
+// MMA thread issues M=256, N=256 MMAs that read both CTAs' tiles, and each
+// CTA's TMEM receives its own 128 accumulator rows (two 256-column buffers).
+// Both CTAs' loads complete their bytes on the even CTA's "stage full"
+// barrier (armed once with both CTAs' bytes); the MMA thread commits "stage
+// empty" and "accumulator full" to the barriers of both CTAs; one lane per
+// epilogue warp of either CTA arrives on the even CTA's "accumulator empty".
+
+template <int kStages>
+struct PairCfg {
+    static constexpr int kTileM = 256, kTileN = 256;
+    static constexpr uint32_t kABytes = 128u * 128u;        // 128 rows x 64 halves
+    static constexpr uint32_t kBBytes = 128u * 128u;        // 64 k-rows x 128 halves
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kBarBytes = 256;
+    static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
+    static constexpr uint32_t kTmemCols = 512;              // 2 x 256 FP32 columns
+    static constexpr uint32_t kIdesc = make_idesc_f16(256, 256, false, true);
+    static_assert(2 * kStages + 5 <= 30, "barrier area");
+    static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+template <int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                  const GemmParams p) {
+    using Cfg = PairCfg<kStages>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align_1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);   // even CTA
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;      // [2]
+    uint64_t* tempty = tfull + 2;           // [2], even CTA
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_index();
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();   // 0 = MMA CTA, 1 = peer
+    const bool leader = rank == 0;
+
+    if (warp == 4 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1u);
+            mbar_init(&empty[s], 1u);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1u);
+            mbar_init(&tempty[i], 8u);     // one lane of each epilogue warp, both CTAs
+        }
+        mbar_init(drain, 1u);
+        *abort_flag = 0;
+        mbar_init_fence();
+        tma_prefetch_map(&tm_a);
+        tma_prefetch_map(&tm_b);
+    }
+    if (warp == 5) {
+        tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync();                       // both CTAs' barriers exist before any remote op
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+    const int tiles_m = (p.m + Cfg::kTileM - 1) / Cfg::kTileM;
+    const int tiles_n = (p.n + Cfg::kTileN - 1) / Cfg::kTileN;
+    const int num_tiles = tiles_m * tiles_n;
+    const int nkb = (p.k + kBlockK - 1) / kBlockK;
+    const int pair = blockIdx.x >> 1;
+    const int npairs = gridDim.x >> 1;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += npairs) {
+                int tm, tn;
+                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+                const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * 128;
+                const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * 128;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
+                    uint8_t* s_a = smem + stage * Cfg::kStageBytes;
+                    uint8_t* s_b = s_a + Cfg::kABytes;
+                    const uint32_t bar = map_to_rank(smem_addr(&full[stage]), 0);
+                    if (leader) {
+                        const uint32_t extra = (p.inject && issued == 0) ? 16u : 0u;
+                        mbar_arrive_expect_tx(&full[stage], 2u * Cfg::kStageBytes + extra);
+                    }
+                    tma_load_2d_pair(s_a, &tm_a, bar, kb * kBlockK, row0);
+                    tma_load_2d_pair(s_b, &tm_b, bar, col0, kb * kBlockK);
+                    tma_load_2d_pair(s_b + kChunkBytes, &tm_b, bar, col0 + 64, kb * kBlockK);
+                    ++issued;
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (leader && (!ok || *abort_flag)) drain_tma<kStages>(full, issued);
+        }
+    } else if (warp == 5) {
+        if (lane == 0 && leader) {
+            uint32_t stage = 0, phase = 0, iter = 0;
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += npairs, ++iter) {
+                const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, wc)) { ok = false; break; }
+                tc_fence_after_sync();
+                const uint32_t d = tmem_base + acc * Cfg::kTileN;
+                for (int kb = 0; kb < nkb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
+                    tc_fence_after_sync();
+                    const uint32_t s_a = smem_addr(smem + stage * Cfg::kStageBytes);
+                    const uint32_t s_b = s_a + Cfg::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 16; ++kk)
+                        tc_mma_f16_pair(d, kmaj_desc(s_a, kk), mnmaj_desc(s_b, kk), Cfg::kIdesc,
+                                        (kb > 0 || kk > 0) ? 1u : 0u);
+                    const uint32_t e = smem_addr(&empty[stage]);
+                    tc_commit_pair(e);
+                    tc_commit_pair(map_to_rank(e, 1));
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) {
+                    const uint32_t f = smem_addr(&tfull[acc]);
+                    tc_commit_pair(f);
+                    tc_commit_pair(map_to_rank(f, 1));
+                }
+            }
+            if (!ok) {
+                tc_commit_pair(smem_addr(drain));
+                mbar_wait_drain(drain, 0, kDrainLimitNs);
+            }
+        }
+    } else {
+        const uint32_t t_lane = (warp * 32u) << 16;
+        const uint32_t tempty_leader0 = map_to_rank(smem_addr(&tempty[0]), 0);
+        const uint32_t tempty_leader1 = map_to_rank(smem_addr(&tempty[1]), 0);
+        uint32_t iter = 0;
+        for (int t = pair; t < num_tiles; t += npairs, ++iter) {
+            const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tfull[acc], acc_phase, wc))) break;
+            tc_fence_after_sync();
+            int tm, tn;
+            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+            const int row = tm * Cfg::kTileM + static_cast<int>(rank) * 128 + warp * 32 + lane;
+            const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kTileN;
+#pragma unroll 1
+            for (int c = 0; c < Cfg::kTileN; c += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(t_acc + c, v);
+                tmem_wait_ld();
+                store_row_segment<32>(p, row, tn * Cfg::kTileN + c, v);
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+        }
+    }
+
+    __syncwarp();
+    // An aborted pipeline may leave the peer's copies in flight towards the
+    // even CTA's barrier; give them time to land before either CTA exits.
+    if (*abort_flag) settle_ns(2000000ull);
+    tc_fence_before_sync();
+    cluster_sync();                       // no CTA leaves while its pair may still touch it
+    if (warp == 5) {
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
 }  // namespace hgemm

@@ -34,6 +34,7 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_splitk_128x128",
     "tc_swapab",
     "tc_generic_128x128",
+    "tc_pair_256x256",
 };
 
 // ------------------------------------------------------ device properties --
@@ -170,12 +171,17 @@ int prepare_kernel(KernelEntry& k, int dev) {
         reinterpret_cast<const void*>(&hgemm_tile_kernel<BN, SWAP, TMA, ST>),              \
             TileCfg<BN, SWAP, TMA, ST>::kSmemBytes                                         \
     }
+#define HG_PAIR(ST)                                                                       \
+    KernelEntry {                                                                          \
+        reinterpret_cast<const void*>(&hgemm_pair_kernel<ST>), PairCfg<ST>::kSmemBytes     \
+    }
 #define HG_PERSIST(BN, ST)                                                                \
     KernelEntry {                                                                          \
         reinterpret_cast<const void*>(&hgemm_persistent_kernel<BN, ST>),                   \
             PersistCfg<BN, ST>::kSmemBytes                                                 \
     }
 
+KernelEntry g_pair_256 = HG_PAIR(6);
 KernelEntry g_persist_256 = HG_PERSIST(256, 4);
 KernelEntry g_persist_128 = HG_PERSIST(128, 6);
 KernelEntry g_splitk_128 = HG_TILE(128, false, true, 6);
@@ -259,16 +265,16 @@ int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, in
 }
 
 int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0, const CUtensorMap& m1,
-           const GemmParams& p, cudaStream_t stream) {
+           const GemmParams& p, cudaStream_t stream, int cluster_x = 1) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
-    if (cluster_z > 1) {
+    if (cluster_z > 1 || cluster_x > 1) {
         attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_x);
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = static_cast<unsigned>(cluster_z);
         cfg.attrs = attr;
@@ -343,6 +349,17 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
             const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, bn);
             const int64_t grid = tiles < dev->sms ? tiles : dev->sms;
             return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_PAIR_256x256: {
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(g_pair_256, devid)) != HGEMM_SM100_OK) return rc;
+            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, 256);
+            const int64_t pairs_max = dev->sms / 2;
+            const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
+            p.group_m = 8;
+            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, p,
+                          stream, 2);
         }
         case HGEMM_SM100_CFG_SPLITK_128x128: {
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;

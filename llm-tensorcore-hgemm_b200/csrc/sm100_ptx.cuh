@@ -247,6 +247,94 @@ __device__ __forceinline__ uint32_t swz128(uint32_t row, uint32_t byte_in_row) {
     return row * 128u + ((((byte_in_row >> 4) ^ (row & 7u)) << 4) | (byte_in_row & 15u));
 }
 
+// ------------------------------------------------- CTA-pair (cta_group::2) ---
+// A pair of CTAs (cluster of 2) shares one MMA: the even CTA issues
+// tcgen05.mma.cta_group::2 with M = 256, reading rows 0-127 of A and columns
+// 0..N/2-1 of B from its own shared memory and the rest from the odd CTA's
+// shared memory at the same offsets; each CTA's TMEM receives its 128 rows.
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_addr(slot)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrives once on the mbarrier at shared::cluster address `bar` (this CTA's
+// or the peer's) when this thread's prior cta_group::2 MMAs have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+
+// 2-D tiled TMA load into this CTA's shared memory whose transaction bytes
+// complete on `bar`, an mbarrier of either CTA of the pair (shared::cluster
+// address). Used so that both CTAs' tiles complete on the MMA CTA's barrier.
+// Plain (not multicast) load of this CTA's own tile.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
+                                                 int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// Sleeps about `ns` nanoseconds (teardown after an aborted pipeline only).
+__device__ __forceinline__ void settle_ns(uint64_t ns) {
+    const uint64_t start = global_timer_ns();
+    while (global_timer_ns() - start < ns) __nanosleep(1000);
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release, cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait with cluster-scope acquire (the barrier is completed by
+// arrivals or commits from the other CTA of the pair).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, const WaitCtl& w) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait_cluster(a, parity)) return true;
+    const uint64_t start = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait_cluster(a, parity)) return true;
+        if ((i & 31u) == 0) {
+            if (*w.abort) return false;
+            if (global_timer_ns() - start > w.timeout_ns) {
+                raise_abort(w, kStatusPipelineTimeout);
+                return false;
+            }
+        }
+    }
+}
+
 // --------------------------------------------------------------- cluster ---
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {

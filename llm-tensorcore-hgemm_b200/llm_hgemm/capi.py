@@ -27,6 +27,7 @@ CFG_PERSISTENT_128x128 = 2
 CFG_SPLITK_128x128 = 3
 CFG_SWAPAB = 4
 CFG_GENERIC_128x128 = 5
+CFG_PAIR_256x256 = 6
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2

@@ -33,6 +33,7 @@ CUSTOM_PROVIDERS = (
     "tc_splitk_128x128",
     "tc_swapab",
     "tc_generic_128x128",
+    "tc_pair_256x256",
 )
 MISALIGNED_PROVIDER = "tc_generic_128x128"
 DEFAULT_PROVIDER = "auto"

@@ -13,6 +13,7 @@ IMPLEMENTATIONS = [
     "tc_splitk_128x128",
     "tc_swapab",
     "tc_generic_128x128",
+    "tc_pair_256x256",
 ]
 
 

@@ -21,6 +21,7 @@ CONFIG_IDS = {
     "tc_splitk_128x128": capi.CFG_SPLITK_128x128,
     "tc_swapab": capi.CFG_SWAPAB,
     "tc_generic_128x128": capi.CFG_GENERIC_128x128,
+    "tc_pair_256x256": capi.CFG_PAIR_256x256,
 }
 
 
