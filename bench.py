@@ -87,70 +87,68 @@ def load_traffic() -> dict:
 
 
 class ClockSampler:
-    """Samples SM clock, power and clock-event reasons through NVML while the
-    timed region runs (read-only queries)."""
+    """Samples SM clock, power and clock-event reasons with ``nvidia-smi
+    --query-gpu ... -lms 100`` while the timed region runs (read-only)."""
 
-    REASONS = {
-        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
-        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
-        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
-        0x100: "display_clock_setting",
-    }
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    FLAGS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
-    def __init__(self, device_index: int, period_s: float = 0.02):
-        self.period = period_s
-        self.samples: list[tuple[int, int, float]] = []
-        self.max_mhz = None
-        self._stop = threading.Event()
-        self._thread = None
-        self._nvml = None
-        try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self._nvml = pynvml
-            self._handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
-        except Exception as exc:  # NVML absent: report no samples
-            log(f"clock sampler unavailable: {exc}")
-            self._nvml = None
-
-    def _run(self) -> None:
-        nv = self._nvml
-        while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
-                power = nv.nvmlDeviceGetPowerUsage(self._handle) / 1000.0
-                self.samples.append((sm, reasons, power))
-            except Exception:
-                pass
-            self._stop.wait(self.period)
+    def __init__(self, device_index: int, period_ms: int = 100):
+        self.device_index = device_index
+        self.period_ms = period_ms
+        self.lines: list[str] = []
+        self._proc = None
 
     def __enter__(self):
-        if self._nvml is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", f"-lms", str(self.period_ms)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)   # let the sampler start before the timed region
+        except OSError as exc:
+            log(f"clock sampler unavailable: {exc}")
+            self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join()
+        if self._proc is not None:
+            time.sleep(0.15)
+            self._proc.terminate()
+            try:
+                out, _ = self._proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+                out, _ = self._proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self) -> dict:
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
-        mask = 0
-        for _, r, _ in self.samples:
-            mask |= r
-        names = sorted({n for bit, n in self.REASONS.items() if mask & bit} - {"gpu_idle"})
+        rows = []
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append({"sm": float(parts[1]), "max": float(parts[2]), "power": float(parts[3]),
+                             "flags": {f: parts[5 + i] == "Active" for i, f in enumerate(self.FLAGS)}})
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        # Samples under load: power well above idle.
+        peak_power = max(r["power"] for r in rows)
+        loaded = [r for r in rows if r["power"] >= 0.5 * peak_power] or rows
+        reasons = sorted({f for r in loaded for f, on in r["flags"].items() if on})
         return {
-            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
-            "sm_max_mhz": self.max_mhz,
-            "reasons": names,
-            "power_w_max": round(max(p for _, _, p in self.samples), 1),
-            "samples": len(self.samples),
+            "sm_mhz": statistics.median(r["sm"] for r in loaded),
+            "sm_max_mhz": max(r["max"] for r in rows),
+            "reasons": reasons,
+            "power_w_max": round(peak_power, 1),
+            "samples": len(rows),
+            "samples_under_load": len(loaded),
+            "source": "nvidia-smi -lms 100",
         }
 
 
@@ -232,28 +230,52 @@ def make_sets(m: int, n: int, k: int, device, nsets: int | None = None, seed: in
 
 
 def median_launch_us(fn_for_set, sets, warmup=20, samples=50, per_sample=10) -> dict:
-    """Reference protocol (docs/benchmark_protocol.md: 20 warm-up, 50 samples of
-    10 launches, CUDA events on the current stream), rotating input sets."""
+    """Reference protocol (docs/benchmark_protocol.md of the reference: 20
+    warm-up launches, 50 samples of 10 launches, CUDA events on the current
+    stream), rotating through input sets larger than L2 in total. Reports the
+    eager timing and the same 10-launch sample replayed as one CUDA graph,
+    which removes host launch overhead (it dominates at decode sizes)."""
     stream = torch.cuda.current_stream()
     idx = 0
     for _ in range(warmup):
         fn_for_set(sets[idx % len(sets)])
         idx += 1
     torch.cuda.synchronize()
-    out = []
-    for _ in range(samples):
-        s = torch.cuda.Event(enable_timing=True)
-        e = torch.cuda.Event(enable_timing=True)
-        s.record(stream)
+
+    def sample(run):
+        out = []
+        for _ in range(samples):
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            run()
+            e.record(stream)
+            e.synchronize()
+            out.append(s.elapsed_time(e) * 1000.0 / per_sample)
+        out.sort()
+        return out
+
+    def eager():
+        nonlocal idx
         for _ in range(per_sample):
             fn_for_set(sets[idx % len(sets)])
             idx += 1
-        e.record(stream)
-        e.synchronize()
-        out.append(s.elapsed_time(e) * 1000.0 / per_sample)
-    out.sort()
-    return {"median_us": statistics.median(out), "p95_us": out[int(0.95 * (len(out) - 1))],
-            "min_us": out[0]}
+
+    eager_us = sample(eager)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for j in range(per_sample):
+                fn_for_set(sets[j % len(sets)])
+    stream.wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize()
+    graph_us = sample(graph.replay)
+    del graph
+    return {"median_us": statistics.median(graph_us), "p95_us": graph_us[int(0.95 * (len(graph_us) - 1))],
+            "min_us": graph_us[0], "eager_median_us": statistics.median(eager_us)}
 
 
 def gpu_reference_check(out, a, b) -> bool:
@@ -296,6 +318,7 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
         rows.append({
             "shape": f"{m}x{n}x{k}", "tag": tag, "config": cfg, "split_k": split,
             "median_us": round(t, 2), "p95_us": round(ours["p95_us"], 2),
+            "eager_median_us": round(ours["eager_median_us"], 2),
             "tflops": round(flops / t / 1e6, 1),
             "pct_of_peak": round(100.0 * flops / t / 1e6 / peak_t, 1),
             "hbm_gbs": round(bytes_ / t / 1e3, 1),
@@ -303,6 +326,7 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
             "roofline_frac": round((flops / t / 1e6 / peak_t) if compute_bound
                                    else (bytes_ / t / 1e3 / peak_bw), 3),
             "cublaslt_us": round(lt["median_us"], 2),
+            "cublaslt_eager_us": round(lt["eager_median_us"], 2),
             "ratio_to_cublaslt": round(lt["median_us"] / t, 3),
             "status": "pass" if ok else "fail",
         })
@@ -377,6 +401,7 @@ def run_square(args, peaks, peak_kind) -> dict:
                    "parallelism": "single GPU"},
         "roofline": {"bound": "tensor", "achieved": round(value, 1), "peak": peak,
                      "unit": "TFLOP/s", "frac": round(value / peak, 4), "traffic": traffic,
+                     "frac_of_sustained": round(value / peaks.get("bf16_tflops_sustained", peak), 4),
                      "peak_source": f"{peak_kind} bf16 burst (MEASURED_PEAKS.json)"
                      if peak_kind == "measured" else "fallback 1.59 PFLOP/s burst",
                      "kernel": cfg},
@@ -494,7 +519,7 @@ def run_reference_arm(args, workload: tuple[int, int, int], world: int) -> dict:
 def main() -> None:
     parser = argparse.ArgumentParser(description="HGEMM benchmark (one JSON line)")
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--steps", type=int, default=1000)
     parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--implementation", default="auto", help="llm_hgemm implementation name")

@@ -14,7 +14,8 @@
  *      cudaStream_t)`, one per backend)                -> hgemm_sm100_run
  *   - csrc/dispatch.cpp:30-32 (`auto` -> backend) and :58-95 (name -> launcher
  *     chain)                       -> hgemm_sm100_config_from_name / _resolve
- *   - csrc/dispatch.cpp:104-128 (`backend_info`)  -> hgemm_sm100_workspace_bytes
+ *   - csrc/dispatch.cpp:104-128 (`backend_info`)  -> hgemm_sm100_workspace_bytes,
+ *                                                    hgemm_sm100_workspace_size
  *   - csrc/dispatch.cpp:99-101 (`has_cutlass`)    -> no counterpart (always 0)
  * Input validation with the reference's messages (csrc/contract.cpp:3-22)
  * stays in the host module; this layer re-checks sizes, strides and
@@ -56,7 +57,8 @@ enum {
     HGEMM_SM100_CFG_GENERIC_128x128 = 5,   /* "tc_generic_128x128": no TMA       */
     HGEMM_SM100_CFG_PAIR_256x256 = 6,      /* "tc_pair_256x256": CTA pair,
                                               cta_group::2, persistent          */
-    HGEMM_SM100_CFG_COUNT = 7
+    HGEMM_SM100_CFG_SPLITK_128x256 = 7,    /* "tc_splitk_128x256": cluster split-K */
+    HGEMM_SM100_CFG_COUNT = 8
 };
 
 /* Flags. */
@@ -79,14 +81,24 @@ typedef struct HgemmSm100Args {
     int32_t* status;     /* optional device int32 the kernel sets on a pipeline
                             timeout; NULL = the library's own status word     */
     uint64_t timeout_ns; /* per-wait limit inside the kernel; 0 = 2 s          */
+    void* workspace;     /* optional device scratch for staging operands that
+                            TMA cannot describe (see hgemm_sm100_workspace_size);
+                            NULL = no staging                                 */
+    uint64_t workspace_bytes;
 } HgemmSm100Args;
 
 /* Launches C = A @ B on `stream` (a cudaStream_t; NULL = legacy default) on
- * the current device. Explicit TMA configurations whose operands TMA cannot
- * describe (a base not 16-byte aligned, or lda / ldb not a multiple of 8) run
- * the generic configuration instead, as the reference's v6 kernels fall back
- * to v5 (csrc/v6_mma_async.cu:428-437). Returns HGEMM_SM100_OK or an error;
- * device-side pipeline timeouts are reported through the status word. */
+ * the current device. TMA needs 16-byte-aligned bases and leading dimensions
+ * that are multiples of 8 halves. For operands that break this (ragged
+ * shapes such as N = 8193, or offset views):
+ *   - with a workspace of at least hgemm_sm100_workspace_size(args) bytes,
+ *     the offending operands are first copied (stream-ordered) into aligned,
+ *     padded staging buffers in the workspace, the TMA kernels run on those,
+ *     and a staged C is copied back;
+ *   - without one, the generic (no-TMA) configuration runs, as the
+ *     reference's v6 kernels fall back to v5 (csrc/v6_mma_async.cu:428-437).
+ * Returns HGEMM_SM100_OK or an error; device-side pipeline timeouts are
+ * reported through the status word. */
 int hgemm_sm100_run(const HgemmSm100Args* args, void* stream);
 
 /* The configuration and K split that hgemm_sm100_run would launch for
@@ -98,10 +110,16 @@ int32_t hgemm_sm100_config_from_name(const char* name);
 const char* hgemm_sm100_config_name(int32_t config);
 int32_t hgemm_sm100_num_configs(void);
 
-/* Global-memory workspace a configuration needs: always 0 (split-K partials
- * are reduced through distributed shared memory). Counterpart of
- * backend_info()["workspace_bytes"] (reference csrc/dispatch.cpp:104-128). */
+/* Global-memory workspace a configuration needs for operands that satisfy
+ * the TMA rules: always 0 (split-K partials are reduced through distributed
+ * shared memory). Counterpart of backend_info()["workspace_bytes"]
+ * (reference csrc/dispatch.cpp:104-128). */
 size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k);
+
+/* Workspace bytes hgemm_sm100_run needs to stage the operands of `args`
+ * that TMA cannot describe (0 when none needs staging, or for the generic
+ * configuration). Pure host computation; no CUDA call. */
+size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
 
 /* Human-readable text of a status code. */
 const char* hgemm_sm100_status_string(int status);

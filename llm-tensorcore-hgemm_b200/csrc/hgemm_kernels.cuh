@@ -177,6 +177,45 @@ __device__ __forceinline__ void load_mnmaj_generic(uint8_t* dst, const __half* y
     }
 }
 
+// ---------------------------------------------------- operand staging ----
+
+// Copies a row-major FP16 [rows x cols] matrix between row pitches. Grid y
+// walks rows, grid x and the threads walk 8-element column chunks, so a warp
+// covers 256 consecutive elements of one row on both sides (coalesced).
+// kDstAligned: the destination base is 16-byte aligned and its pitch a
+// multiple of 8, so each thread writes one 16-byte vector (zero-filling the
+// row padding); otherwise the destination is written element by element and
+// the source (then the aligned side) read as one 16-byte vector.
+template <bool kDstAligned>
+__global__ void __launch_bounds__(256)
+copy_rows_kernel(const __half* __restrict__ src, long long ld_src, __half* __restrict__ dst,
+                 long long ld_dst, long long rows, long long cols) {
+    const long long col_step = static_cast<long long>(gridDim.x) * blockDim.x * 8;
+    for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+        const __half* srow = src + r * ld_src;
+        __half* drow = dst + r * ld_dst;
+        for (long long c = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; c < cols;
+             c += col_step) {
+            __align__(16) __half v[8];
+            if constexpr (kDstAligned) {
+                if (c + 8 <= cols) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = __ldg(srow + c + j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = (c + j < cols) ? __ldg(srow + c + j) : __float2half_rn(0.f);
+                }
+                *reinterpret_cast<uint4*>(drow + c) = *reinterpret_cast<const uint4*>(v);
+            } else {
+                *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(srow + c));
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (c + j < cols) drow[c + j] = v[j];
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------- descriptors ----
 
 __device__ __forceinline__ uint64_t kmaj_desc(uint32_t tile, int kk) {

@@ -35,6 +35,7 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_swapab",
     "tc_generic_128x128",
     "tc_pair_256x256",
+    "tc_splitk_128x256",
 };
 
 // ------------------------------------------------------ device properties --
@@ -185,31 +186,31 @@ KernelEntry g_pair_256 = HG_PAIR(6);
 KernelEntry g_persist_256 = HG_PERSIST(256, 4);
 KernelEntry g_persist_128 = HG_PERSIST(128, 6);
 KernelEntry g_splitk_128 = HG_TILE(128, false, true, 6);
+KernelEntry g_splitk_256 = HG_TILE(256, false, true, 4);
 KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
-KernelEntry g_swap_16 = HG_TILE(16, true, true, 8);
-KernelEntry g_swap_32 = HG_TILE(32, true, true, 8);
-KernelEntry g_swap_64 = HG_TILE(64, true, true, 6);
-KernelEntry g_swap_128 = HG_TILE(128, true, true, 5);
+// Swap-AB tiles for M <= 128 use at most ~110 KB of shared memory so that two
+// CTAs (of different clusters) share an SM; their TMEM (<= 128 columns
+// each) then fits twice into the 512 columns.
+KernelEntry g_swap_16 = HG_TILE(16, true, true, 6);
+KernelEntry g_swap_32 = HG_TILE(32, true, true, 5);
+KernelEntry g_swap_64 = HG_TILE(64, true, true, 4);
+KernelEntry g_swap_128 = HG_TILE(128, true, true, 3);
 KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
 
 struct SwapChoice {
     int bnm;
     KernelEntry* k;
+    int per_sm;   // CTAs that fit on one SM
 };
 SwapChoice swap_choice(int64_t m) {
-    if (m <= 16) return {16, &g_swap_16};
-    if (m <= 32) return {32, &g_swap_32};
-    if (m <= 64) return {64, &g_swap_64};
-    if (m <= 128) return {128, &g_swap_128};
-    return {256, &g_swap_256};
+    if (m <= 16) return {16, &g_swap_16, 2};
+    if (m <= 32) return {32, &g_swap_32, 2};
+    if (m <= 64) return {64, &g_swap_64, 2};
+    if (m <= 128) return {128, &g_swap_128, 2};
+    return {256, &g_swap_256, 1};
 }
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
-
-bool tma_eligible(const HgemmSm100Args& a) {
-    return (reinterpret_cast<uintptr_t>(a.a) % 16 == 0) && (reinterpret_cast<uintptr_t>(a.b) % 16 == 0) &&
-           (a.lda % 8 == 0) && (a.ldb % 8 == 0);
-}
 
 // K splits for a tile kernel: enough clusters to cover the SMs once, at most
 // one K block per split, at most the cluster limit.
@@ -233,29 +234,88 @@ int check_args(const HgemmSm100Args* a) {
     return HGEMM_SM100_OK;
 }
 
+// Operand staging: TMA needs 16-byte-aligned bases and row pitches that are
+// multiples of 8 halves (16 bytes). Operands breaking this are copied into
+// padded, aligned buffers carved from the caller's workspace.
+struct Staging {
+    bool a = false, b = false, c = false;
+    int64_t lda = 0, ldb = 0, ldc = 0;      // pitches of the staged copies
+    size_t off_a = 0, off_b = 0, off_c = 0, total = 0;
+};
+
+constexpr size_t kStageAlign = 256;
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+bool fp16_tma_ok(const void* ptr, int64_t ld) {
+    return reinterpret_cast<uintptr_t>(ptr) % 16 == 0 && ld % 8 == 0;
+}
+
+Staging plan_staging(const HgemmSm100Args& a) {
+    Staging st;
+    if (a.config == HGEMM_SM100_CFG_GENERIC_128x128) return st;
+    st.a = !fp16_tma_ok(a.a, a.lda);
+    st.b = !fp16_tma_ok(a.b, a.ldb);
+    const bool out_f32 = (a.flags & HGEMM_SM100_FLAG_OUT_F32) != 0;
+    // A ragged FP16 C is computed into an aligned copy (16-byte epilogue
+    // stores) and copied out; an FP32 C is never staged.
+    st.c = !out_f32 && !fp16_tma_ok(a.c, a.ldc);
+    size_t off = 0;
+    if (st.a) {
+        st.lda = static_cast<int64_t>(align_up(a.k, 8));
+        st.off_a = off;
+        off = align_up(off + static_cast<size_t>(a.m) * st.lda * 2, kStageAlign);
+    }
+    if (st.b) {
+        st.ldb = static_cast<int64_t>(align_up(a.n, 8));
+        st.off_b = off;
+        off = align_up(off + static_cast<size_t>(a.k) * st.ldb * 2, kStageAlign);
+    }
+    if (st.c) {
+        st.ldc = static_cast<int64_t>(align_up(a.n, 8));
+        st.off_c = off;
+        off = align_up(off + static_cast<size_t>(a.m) * st.ldc * 2, kStageAlign);
+    }
+    st.total = off;
+    return st;
+}
+
+bool staging_usable(const HgemmSm100Args& a, const Staging& st) {
+    return st.total > 0 && a.workspace != nullptr && a.workspace_bytes >= st.total &&
+           reinterpret_cast<uintptr_t>(a.workspace) % kStageAlign == 0;
+}
+
 int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, int32_t* split_out) {
     int32_t cfg = a.config;
     const int64_t nkb = cdiv(a.k, kBlockK);
     const int sms = dev.sms > 0 ? dev.sms : 148;
-    if (!tma_eligible(a)) {
+    const Staging st = plan_staging(a);
+    const bool ab_ready = !(st.a || st.b) || staging_usable(a, st);
+    if (!ab_ready) {
         cfg = HGEMM_SM100_CFG_GENERIC_128x128;
     } else if (cfg == HGEMM_SM100_CFG_AUTO) {
         const int64_t tiles_256 = cdiv(a.m, 128) * cdiv(a.n, 256);
-        const int64_t tiles_128 = cdiv(a.m, 128) * cdiv(a.n, 128);
         if (a.m <= 256) cfg = HGEMM_SM100_CFG_SWAPAB;
-        else if (tiles_256 >= 2 * sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x256;
-        else if (tiles_128 >= sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x128;
-        else cfg = HGEMM_SM100_CFG_SPLITK_128x128;
+        else if (4 * tiles_256 >= 3 * sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x256;
+        else cfg = HGEMM_SM100_CFG_SPLITK_128x256;
     }
-    if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x128;
+    if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x256;
 
     int32_t split = 1;
-    if (cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_GENERIC_128x128 ||
-        cfg == HGEMM_SM100_CFG_SWAPAB) {
+    if (cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_SPLITK_128x256 ||
+        cfg == HGEMM_SM100_CFG_GENERIC_128x128 || cfg == HGEMM_SM100_CFG_SWAPAB) {
         int64_t base;
-        if (cfg == HGEMM_SM100_CFG_SWAPAB) base = cdiv(a.n, 128) * cdiv(a.m, swap_choice(a.m).bnm);
-        else base = cdiv(a.m, 128) * cdiv(a.n, 128);
-        split = a.split_k > 0 ? a.split_k : choose_split(base, nkb, sms, dev.max_cluster);
+        int per_sm = 1;
+        if (cfg == HGEMM_SM100_CFG_SWAPAB) {
+            const SwapChoice sc = swap_choice(a.m);
+            base = cdiv(a.n, 128) * cdiv(a.m, sc.bnm);
+            per_sm = sc.per_sm;
+        } else if (cfg == HGEMM_SM100_CFG_SPLITK_128x256) {
+            base = cdiv(a.m, 128) * cdiv(a.n, 256);
+        } else {
+            base = cdiv(a.m, 128) * cdiv(a.n, 128);
+        }
+        split = a.split_k > 0 ? a.split_k : choose_split(base, nkb, sms * per_sm, dev.max_cluster);
         if (split > nkb) split = static_cast<int32_t>(nkb);
         if (split < 1) split = 1;
     }
@@ -285,6 +345,107 @@ int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0
     return e == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
 }
 
+int launch_copy(const __half* src, int64_t ld_src, __half* dst, int64_t ld_dst, int64_t rows,
+                int64_t cols, bool dst_aligned, int sms, cudaStream_t stream) {
+    // ~8 blocks of 256 threads per SM in flight; x covers a row's chunks.
+    int64_t bx = cdiv(cdiv(cols, 8), 256);
+    if (bx > 64) bx = 64;
+    int64_t by = cdiv(static_cast<int64_t>(sms) * 8, bx);
+    if (by > rows) by = rows;
+    if (by > 65535) by = 65535;
+    const dim3 grid(static_cast<unsigned>(bx), static_cast<unsigned>(by), 1);
+    if (dst_aligned)
+        copy_rows_kernel<true><<<grid, 256, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+    else
+        copy_rows_kernel<false><<<grid, 256, 0, stream>>>(src, ld_src, dst, ld_dst, rows, cols);
+    return cudaGetLastError() == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
+}
+
+// Launches the resolved configuration on operands that TMA can describe
+// (or, for the generic configuration, on any operands).
+int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceInfo& dev, int devid,
+             cudaStream_t stream) {
+    int rc = HGEMM_SM100_OK;
+    GemmParams p{};
+    p.a = static_cast<const __half*>(a.a);
+    p.b = static_cast<const __half*>(a.b);
+    p.c = a.c;
+    p.m = static_cast<int>(a.m);
+    p.n = static_cast<int>(a.n);
+    p.k = static_cast<int>(a.k);
+    p.lda = a.lda;
+    p.ldb = a.ldb;
+    p.ldc = a.ldc;
+    p.out_f32 = (a.flags & HGEMM_SM100_FLAG_OUT_F32) ? 1 : 0;
+    p.vec_ok = (reinterpret_cast<uintptr_t>(a.c) % 16 == 0) && (a.ldc % 8 == 0);
+    p.group_m = 16;
+    p.inject = (a.flags & HGEMM_SM100_FLAG_TEST_INJECT_TX) ? 1 : 0;
+    p.status = a.status != nullptr ? a.status : dev.status_word;
+    p.timeout_ns = a.timeout_ns != 0 ? a.timeout_ns : kDefaultTimeoutNs;
+
+    CUtensorMap map_k, map_mn;
+    std::memset(&map_k, 0, sizeof(map_k));
+    std::memset(&map_mn, 0, sizeof(map_mn));
+    const uint64_t M = a.m, N = a.n, K = a.k;
+
+    switch (cfg) {
+        case HGEMM_SM100_CFG_PERSISTENT_128x256:
+        case HGEMM_SM100_CFG_PERSISTENT_128x128: {
+            const bool wide = cfg == HGEMM_SM100_CFG_PERSISTENT_128x256;
+            KernelEntry& k = wide ? g_persist_256 : g_persist_128;
+            const int bn = wide ? 256 : 128;
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
+            const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, bn);
+            const int64_t grid = tiles < dev.sms ? tiles : dev.sms;
+            return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_PAIR_256x256: {
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(g_pair_256, devid)) != HGEMM_SM100_OK) return rc;
+            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, 256);
+            const int64_t pairs_max = dev.sms / 2;
+            const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
+            p.group_m = 8;
+            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, p,
+                          stream, 2);
+        }
+        case HGEMM_SM100_CFG_SPLITK_128x128:
+        case HGEMM_SM100_CFG_SPLITK_128x256: {
+            const bool wide = cfg == HGEMM_SM100_CFG_SPLITK_128x256;
+            KernelEntry& k = wide ? g_splitk_256 : g_splitk_128;
+            const int bn = wide ? 256 : 128;
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, bn)),
+                            static_cast<unsigned>(split));
+            return launch(k, grid, split, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_SWAPAB: {
+            const SwapChoice sc = swap_choice(a.m);
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(sc.bnm))) !=
+                HGEMM_SM100_OK)
+                return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(*sc.k, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
+                            static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
+            return launch(*sc.k, grid, split, map_k, map_mn, p, stream);
+        }
+        case HGEMM_SM100_CFG_GENERIC_128x128: {
+            if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
+            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
+                            static_cast<unsigned>(split));
+            return launch(g_generic_128, grid, split, map_k, map_mn, p, stream);
+        }
+        default:
+            return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    }
+}
+
 }  // namespace
 
 // ================================================================== C ABI ==
@@ -307,88 +468,51 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     if (rc != HGEMM_SM100_OK) return rc;
     int devid = 0;
     cudaGetDevice(&devid);
-    const HgemmSm100Args& a = *args;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
 
     int32_t cfg = 0, split = 1;
-    rc = resolve(a, *dev, &cfg, &split);
+    rc = resolve(*args, *dev, &cfg, &split);
     if (rc != HGEMM_SM100_OK) return rc;
 
-    GemmParams p{};
-    p.a = static_cast<const __half*>(a.a);
-    p.b = static_cast<const __half*>(a.b);
-    p.c = a.c;
-    p.m = static_cast<int>(a.m);
-    p.n = static_cast<int>(a.n);
-    p.k = static_cast<int>(a.k);
-    p.lda = a.lda;
-    p.ldb = a.ldb;
-    p.ldc = a.ldc;
-    p.out_f32 = (a.flags & HGEMM_SM100_FLAG_OUT_F32) ? 1 : 0;
-    const uintptr_t c_align = p.out_f32 ? 16 : 16;
-    p.vec_ok = (reinterpret_cast<uintptr_t>(a.c) % c_align == 0) && (a.ldc % 8 == 0);
-    p.group_m = 16;
-    p.inject = (a.flags & HGEMM_SM100_FLAG_TEST_INJECT_TX) ? 1 : 0;
-    p.status = a.status != nullptr ? a.status : dev->status_word;
-    p.timeout_ns = a.timeout_ns != 0 ? a.timeout_ns : kDefaultTimeoutNs;
+    const Staging st = plan_staging(*args);
+    if (cfg == HGEMM_SM100_CFG_GENERIC_128x128 || !staging_usable(*args, st))
+        return run_core(*args, cfg, split, *dev, devid, stream);
 
-    CUtensorMap map_k, map_mn;
-    std::memset(&map_k, 0, sizeof(map_k));
-    std::memset(&map_mn, 0, sizeof(map_mn));
-    const uint64_t M = a.m, N = a.n, K = a.k;
-
-    switch (cfg) {
-        case HGEMM_SM100_CFG_PERSISTENT_128x256:
-        case HGEMM_SM100_CFG_PERSISTENT_128x128: {
-            const bool wide = cfg == HGEMM_SM100_CFG_PERSISTENT_128x256;
-            KernelEntry& k = wide ? g_persist_256 : g_persist_128;
-            const int bn = wide ? 256 : 128;
-            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
-            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
-            if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
-            const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, bn);
-            const int64_t grid = tiles < dev->sms ? tiles : dev->sms;
-            return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, p, stream);
-        }
-        case HGEMM_SM100_CFG_PAIR_256x256: {
-            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
-            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
-            if ((rc = prepare_kernel(g_pair_256, devid)) != HGEMM_SM100_OK) return rc;
-            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, 256);
-            const int64_t pairs_max = dev->sms / 2;
-            const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
-            p.group_m = 8;
-            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, p,
-                          stream, 2);
-        }
-        case HGEMM_SM100_CFG_SPLITK_128x128: {
-            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
-            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
-            if ((rc = prepare_kernel(g_splitk_128, devid)) != HGEMM_SM100_OK) return rc;
-            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
-                            static_cast<unsigned>(split));
-            return launch(g_splitk_128, grid, split, map_k, map_mn, p, stream);
-        }
-        case HGEMM_SM100_CFG_SWAPAB: {
-            const SwapChoice sc = swap_choice(a.m);
-            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(sc.bnm))) !=
-                HGEMM_SM100_OK)
-                return rc;
-            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
-            if ((rc = prepare_kernel(*sc.k, devid)) != HGEMM_SM100_OK) return rc;
-            const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
-                            static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
-            return launch(*sc.k, grid, split, map_k, map_mn, p, stream);
-        }
-        case HGEMM_SM100_CFG_GENERIC_128x128: {
-            if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
-            const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
-                            static_cast<unsigned>(split));
-            return launch(g_generic_128, grid, split, map_k, map_mn, p, stream);
-        }
-        default:
-            return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    // Stage, run on the staged operands, copy a staged C back.
+    HgemmSm100Args s = *args;
+    uint8_t* ws = static_cast<uint8_t*>(args->workspace);
+    if (st.a) {
+        __half* dst = reinterpret_cast<__half*>(ws + st.off_a);
+        if ((rc = launch_copy(static_cast<const __half*>(args->a), args->lda, dst, st.lda, args->m, args->k,
+                              true, dev->sms, stream)) != HGEMM_SM100_OK)
+            return rc;
+        s.a = dst;
+        s.lda = st.lda;
     }
+    if (st.b) {
+        __half* dst = reinterpret_cast<__half*>(ws + st.off_b);
+        if ((rc = launch_copy(static_cast<const __half*>(args->b), args->ldb, dst, st.ldb, args->k, args->n,
+                              true, dev->sms, stream)) != HGEMM_SM100_OK)
+            return rc;
+        s.b = dst;
+        s.ldb = st.ldb;
+    }
+    if (st.c) {
+        s.c = ws + st.off_c;
+        s.ldc = st.ldc;
+    }
+    s.config = cfg;
+    s.split_k = split;
+    if ((rc = run_core(s, cfg, split, *dev, devid, stream)) != HGEMM_SM100_OK) return rc;
+    if (st.c)
+        return launch_copy(static_cast<const __half*>(s.c), st.ldc, static_cast<__half*>(args->c), args->ldc,
+                           args->m, args->n, false, dev->sms, stream);
+    return HGEMM_SM100_OK;
+}
+
+extern "C" size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args) {
+    if (check_args(args) != HGEMM_SM100_OK) return 0;
+    return plan_staging(*args).total;
 }
 
 extern "C" int32_t hgemm_sm100_config_from_name(const char* name) {

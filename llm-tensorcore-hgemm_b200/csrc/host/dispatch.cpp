@@ -43,6 +43,8 @@ HgemmSm100Args make_args(const torch::Tensor& a, const torch::Tensor& b, const t
     args.flags = flags;
     args.status = nullptr;
     args.timeout_ns = 0;
+    args.workspace = nullptr;
+    args.workspace_bytes = 0;
     return args;
 }
 
@@ -50,7 +52,19 @@ void run(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, con
          int32_t cfg, int32_t flags) {
     const c10::cuda::CUDAGuard device_guard(a.device());
     const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(p.device).stream();
-    const HgemmSm100Args args = make_args(a, b, out, p, cfg, flags);
+    HgemmSm100Args args = make_args(a, b, out, p, cfg, flags);
+    // Operands TMA cannot describe (offset views; pitches not a multiple of 8
+    // halves) are staged in a workspace from the caching allocator. It is
+    // allocated on the current stream, so its reuse is stream-ordered after
+    // the kernels that read it.
+    torch::Tensor workspace;
+    const size_t ws = hgemm_sm100_workspace_size(&args);
+    if (ws > 0) {
+        workspace = torch::empty({static_cast<int64_t>(ws)},
+                                 torch::TensorOptions().dtype(torch::kUInt8).device(a.device()));
+        args.workspace = workspace.data_ptr();
+        args.workspace_bytes = ws;
+    }
     const int rc = hgemm_sm100_run(&args, stream);
     TORCH_CHECK(rc == HGEMM_SM100_OK, "hgemm_sm100_run failed: ", hgemm_sm100_status_string(rc));
 }
@@ -104,6 +118,10 @@ std::tuple<std::string, int64_t> resolve(const torch::Tensor& a, const torch::Te
     torch::Tensor none;
     HgemmSm100Args args = make_args(a, b, none, problem, cfg, 0);
     args.c = a.data_ptr();  // only checked for non-null; nothing is launched
+    // As hgemm_out would: a staging workspace whenever one is needed (its
+    // address is not used by resolution).
+    args.workspace_bytes = hgemm_sm100_workspace_size(&args);
+    if (args.workspace_bytes > 0) args.workspace = reinterpret_cast<void*>(uintptr_t{256});
     int32_t resolved = 0, split = 0;
     const int rc = hgemm_sm100_resolve(&args, &resolved, &split);
     TORCH_CHECK(rc == HGEMM_SM100_OK, "hgemm_sm100_resolve failed: ", hgemm_sm100_status_string(rc));

@@ -28,6 +28,7 @@ CFG_SPLITK_128x128 = 3
 CFG_SWAPAB = 4
 CFG_GENERIC_128x128 = 5
 CFG_PAIR_256x256 = 6
+CFG_SPLITK_128x256 = 7
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2
@@ -49,6 +50,8 @@ class HgemmSm100Args(ctypes.Structure):
         ("flags", ctypes.c_int32),
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -74,6 +77,8 @@ def load() -> ctypes.CDLL:
         lib.hgemm_sm100_workspace_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64,
                                                     ctypes.c_int64, ctypes.c_int64]
         lib.hgemm_sm100_workspace_bytes.restype = ctypes.c_size_t
+        lib.hgemm_sm100_workspace_size.argtypes = [ctypes.POINTER(HgemmSm100Args)]
+        lib.hgemm_sm100_workspace_size.restype = ctypes.c_size_t
         lib.hgemm_sm100_status_string.argtypes = [ctypes.c_int]
         lib.hgemm_sm100_status_string.restype = ctypes.c_char_p
         lib.hgemm_sm100_read_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int]
@@ -85,11 +90,12 @@ def load() -> ctypes.CDLL:
 def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
               lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
               config: int = CFG_AUTO, split_k: int = 0, flags: int = 0,
-              status_ptr: int | None = None, timeout_ns: int = 0) -> HgemmSm100Args:
+              status_ptr: int | None = None, timeout_ns: int = 0,
+              workspace_ptr: int | None = None, workspace_bytes: int = 0) -> HgemmSm100Args:
     return HgemmSm100Args(a_ptr, b_ptr, c_ptr, m, n, k,
                           k if lda is None else lda, n if ldb is None else ldb,
                           n if ldc is None else ldc, config, split_k, flags,
-                          status_ptr, timeout_ns)
+                          status_ptr, timeout_ns, workspace_ptr, workspace_bytes)
 
 
 def run(args: HgemmSm100Args, stream: int = 0) -> int:
@@ -100,6 +106,10 @@ def resolve(args: HgemmSm100Args) -> tuple[int, int, int]:
     cfg, split = ctypes.c_int32(0), ctypes.c_int32(0)
     rc = load().hgemm_sm100_resolve(ctypes.byref(args), ctypes.byref(cfg), ctypes.byref(split))
     return rc, cfg.value, split.value
+
+
+def workspace_size(args: HgemmSm100Args) -> int:
+    return load().hgemm_sm100_workspace_size(ctypes.byref(args))
 
 
 def status_string(code: int) -> str:

@@ -11,7 +11,8 @@ returns the requested name unchanged unless it is ``shape_auto``; then:
 * inputs that break the contract -> ``auto`` (the C++ layer raises the error);
 * no policy, or an ineligible device -> ``auto`` (the SM100 shape heuristic;
   the reference fell back to cuBLASLt, which is not a dispatch target here);
-* a base address not 16-byte aligned -> ``tc_generic_128x128`` (no TMA);
+* a base address not 16-byte aligned -> ``auto`` (a table entry was tuned on
+  aligned operands; ``auto`` stages such operands for TMA);
 * otherwise the table entry for (M, N, K), else ``auto``.
 
 The last selection is recorded per thread (``record_selected``/``last_selected``).
@@ -34,8 +35,9 @@ CUSTOM_PROVIDERS = (
     "tc_swapab",
     "tc_generic_128x128",
     "tc_pair_256x256",
+    "tc_splitk_128x256",
 )
-MISALIGNED_PROVIDER = "tc_generic_128x128"
+MISALIGNED_PROVIDER = "auto"
 DEFAULT_PROVIDER = "auto"
 SCHEMA_VERSION = 3
 TARGET_SM = "10.0"

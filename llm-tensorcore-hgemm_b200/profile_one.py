@@ -26,6 +26,8 @@ def main() -> None:
     p.add_argument("--n", type=int, required=True)
     p.add_argument("--k", type=int, required=True)
     p.add_argument("--implementation", default="auto")
+    p.add_argument("--provider", choices=["hgemm", "cublaslt"], default="hgemm",
+                   help="cublaslt: the benchmark-only comparator on the same inputs")
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--seed", type=int, default=2026)
@@ -34,6 +36,14 @@ def main() -> None:
     a = torch.randn((args.m, args.k), device="cuda", dtype=torch.float16) * 0.1
     b = torch.randn((args.k, args.n), device="cuda", dtype=torch.float16) * 0.1
     c = torch.empty((args.m, args.n), device="cuda", dtype=torch.float16)
+    if args.provider == "cublaslt":
+        from llm_hgemm import _comparators
+
+        for _ in range(args.warmup + args.iters):
+            _comparators.cublaslt_out(a, b, c)
+        torch.cuda.synchronize()
+        print(f"profiled {args.m}x{args.n}x{args.k} cublaslt comparator")
+        return
     cfg, split = resolved_config(a, b, args.implementation)
     for _ in range(args.warmup + args.iters):
         _hgemm_out(a, b, c, implementation=args.implementation)

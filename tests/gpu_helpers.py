@@ -14,6 +14,7 @@ IMPLEMENTATIONS = [
     "tc_swapab",
     "tc_generic_128x128",
     "tc_pair_256x256",
+    "tc_splitk_128x256",
 ]
 
 

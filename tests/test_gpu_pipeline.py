@@ -22,6 +22,7 @@ CONFIG_IDS = {
     "tc_swapab": capi.CFG_SWAPAB,
     "tc_generic_128x128": capi.CFG_GENERIC_128x128,
     "tc_pair_256x256": capi.CFG_PAIR_256x256,
+    "tc_splitk_128x256": capi.CFG_SPLITK_128x256,
 }
 
 
@@ -59,7 +60,8 @@ def test_stage_markers_every_ring_depth(impl, kblocks, mn):
     torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("config", ["tc_splitk_128x128", "tc_swapab", "tc_generic_128x128"])
+@pytest.mark.parametrize("config", ["tc_splitk_128x128", "tc_splitk_128x256", "tc_swapab",
+                                    "tc_generic_128x128"])
 @pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 8, 16])
 def test_explicit_split_k(config, split):
     m, n, k = (48, 384, 64 * 17) if config == "tc_swapab" else (200, 260, 64 * 17)
@@ -147,3 +149,50 @@ def test_capi_matches_module_bitwise():
         out = torch.empty((300, 520), device="cuda", dtype=torch.float16)
         run_capi(a, b, out, cfg)
         assert torch.equal(out, hgemm(a, b, implementation=name)), name
+
+
+STAGED_SHAPES = [(300, 1001, 517), (257, 129, 1003), (37, 53, 29), (1, 8193, 70), (513, 131, 264)]
+
+
+@pytest.mark.parametrize("config", [c for c in CONFIG_IDS if c != "tc_generic_128x128"])
+@pytest.mark.parametrize("shape", STAGED_SHAPES)
+def test_staged_ragged_operands(config, shape):
+    """Pitches that are not multiples of 8 halves: staged through the
+    workspace into aligned copies, then the TMA configuration runs."""
+    m, n, k = shape
+    a, b = seeded_inputs(m, n, k)
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
+                          config=CONFIG_IDS[config])
+    need = capi.workspace_size(args)
+    assert need > 0
+    ws = torch.empty(need, device="cuda", dtype=torch.uint8)
+    args.workspace, args.workspace_bytes = ws.data_ptr(), need
+    rc, cfg, _ = capi.resolve(args)
+    assert rc == capi.OK and cfg == CONFIG_IDS[config] or config == "tc_swapab"
+    assert capi.run(args, torch.cuda.current_stream().cuda_stream) == capi.OK
+    assert_gate(out, a, b)
+    # Without a workspace the same call runs the generic (no-TMA) kernel.
+    out2 = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    args2 = capi.make_args(a.data_ptr(), b.data_ptr(), out2.data_ptr(), m, n, k,
+                           config=CONFIG_IDS[config])
+    rc, cfg, _ = capi.resolve(args2)
+    assert cfg == capi.CFG_GENERIC_128x128
+    assert capi.run(args2, torch.cuda.current_stream().cuda_stream) == capi.OK
+    assert_gate(out2, a, b)
+
+
+@pytest.mark.parametrize("offsets", [(1, 0, 0), (0, 1, 0), (0, 0, 1), (1, 1, 1), (3, 5, 7)])
+def test_staged_offset_views_through_api(offsets):
+    """Offset (misaligned) views through the public API: staged, TMA path."""
+    oa, ob, oc = offsets
+    m, n, k = 200, 264, 520
+    torch.manual_seed(5)
+    sa = torch.randn(m * k + oa, device="cuda", dtype=torch.float16) * 0.1
+    sb = torch.randn(k * n + ob, device="cuda", dtype=torch.float16) * 0.1
+    sc = torch.full((m * n + oc,), float("nan"), device="cuda", dtype=torch.float16)
+    a, b, out = sa[oa:].view(m, k), sb[ob:].view(k, n), sc[oc:].view(m, n)
+    returned = _hgemm_out(a, b, out, implementation="auto")
+    assert returned is out
+    assert_gate(out, a, b)
+    assert torch.all(torch.isnan(sc[:oc])) if oc else True
