@@ -58,7 +58,11 @@ enum {
     HGEMM_SM100_CFG_PAIR_256x256 = 6,      /* "tc_pair_256x256": CTA pair,
                                               cta_group::2, persistent          */
     HGEMM_SM100_CFG_SPLITK_128x256 = 7,    /* "tc_splitk_128x256": cluster split-K */
-    HGEMM_SM100_CFG_COUNT = 8
+    HGEMM_SM100_CFG_STREAMK_128x256 = 8,   /* "tc_streamk_128x256": persistent,
+                                              stream-K ranges (workspace)       */
+    HGEMM_SM100_CFG_STREAMK_SWAPAB = 9,    /* "tc_streamk_swapab": the same with
+                                              C^T = B^T A^T, M <= 128           */
+    HGEMM_SM100_CFG_COUNT = 10
 };
 
 /* Flags. */
@@ -110,15 +114,19 @@ int32_t hgemm_sm100_config_from_name(const char* name);
 const char* hgemm_sm100_config_name(int32_t config);
 int32_t hgemm_sm100_num_configs(void);
 
-/* Global-memory workspace a configuration needs for operands that satisfy
- * the TMA rules: always 0 (split-K partials are reduced through distributed
- * shared memory). Counterpart of backend_info()["workspace_bytes"]
- * (reference csrc/dispatch.cpp:104-128). */
+/* Global-memory workspace a configuration needs independent of the operands'
+ * alignment: 0 for the split-K configurations (partials are reduced through
+ * distributed shared memory); for the stream-K configurations the per-CTA
+ * slots for an (m, n, k) problem on the current device. Counterpart of
+ * backend_info()["workspace_bytes"] (reference csrc/dispatch.cpp:104-128). */
 size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k);
 
-/* Workspace bytes hgemm_sm100_run needs to stage the operands of `args`
- * that TMA cannot describe (0 when none needs staging, or for the generic
- * configuration). Pure host computation; no CUDA call. */
+/* Workspace bytes hgemm_sm100_run needs for `args`: staging buffers for
+ * operands that TMA cannot describe, plus, when the call resolves to a
+ * stream-K configuration, one FP32 partial-tile slot and one flag per CTA.
+ * 0 when neither applies. Queries the current device's SM count (cached);
+ * launches nothing. The stream-K part keeps no state between calls: any
+ * workspace of this size works, whatever it contains. */
 size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
 
 /* Human-readable text of a status code. */

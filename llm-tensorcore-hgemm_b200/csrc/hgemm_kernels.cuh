@@ -64,6 +64,12 @@ struct GemmParams {
     int inject;            // test-only: arm the first stage with 16 extra bytes
     int* status;
     unsigned long long timeout_ns;
+    // Stream-K (hgemm_streamk_kernel only): FP32 partial tiles and their
+    // readiness flags in the caller's workspace, one slot per CTA.
+    float* partials;
+    unsigned long long* flags;
+    unsigned long long epoch;  // this launch's flag value (never 0)
+    int streamk;               // 1: stream-K k-ranges, 0: whole tiles
 };
 
 // ------------------------------------------------------------ epilogue ----
@@ -429,18 +435,40 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
         constexpr uint32_t kQuads = Cfg::kRedRows * kQuadsPerRow;
         const uint32_t q0 = rank * kQuads / split, q1 = (rank + 1) * kQuads / split;
         const uint32_t red_base = smem_addr(smem);
-        for (uint32_t q = q0 + threadIdx.x; q < q1; q += kThreads) {
-            const uint32_t rr = q / kQuadsPerRow, cc = (q % kQuadsPerRow) * 4;
-            const uint32_t off = red_base + (rr * Cfg::kRedStride + cc) * 4u;
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int s = 0; s < split; ++s) {
-                const float4 v = ld_dsmem_f4(map_to_rank(off, s));
-                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        // kUnroll quads per thread and round keep that many remote loads in
+        // flight per rank (the loop is otherwise bound by DSMEM latency).
+        constexpr uint32_t kUnroll = 8;
+        for (uint32_t q = q0 + threadIdx.x; q < q1; q += kThreads * kUnroll) {
+            float4 acc[kUnroll];
+            uint32_t off[kUnroll];
+#pragma unroll
+            for (uint32_t u = 0; u < kUnroll; ++u) {
+                acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                const uint32_t qq = q + u * kThreads;
+                const uint32_t rr = qq / kQuadsPerRow, cc = (qq % kQuadsPerRow) * 4;
+                off[u] = red_base + (rr * Cfg::kRedStride + cc) * 4u;
             }
-            if constexpr (kSwap) {
-                store_quad(p, acc_col0 + rr, acc_row0 + cc, acc);   // row = m, cols = n
-            } else {
-                store_quad(p, acc_row0 + rr, acc_col0 + cc, acc);
+            for (int s = 0; s < split; ++s) {
+                float4 v[kUnroll];
+#pragma unroll
+                for (uint32_t u = 0; u < kUnroll; ++u)
+                    if (q + u * kThreads < q1) v[u] = ld_dsmem_f4(map_to_rank(off[u], s));
+#pragma unroll
+                for (uint32_t u = 0; u < kUnroll; ++u)
+                    if (q + u * kThreads < q1) {
+                        acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
+                    }
+            }
+#pragma unroll
+            for (uint32_t u = 0; u < kUnroll; ++u) {
+                const uint32_t qq = q + u * kThreads;
+                if (qq >= q1) break;
+                const uint32_t rr = qq / kQuadsPerRow, cc = (qq % kQuadsPerRow) * 4;
+                if constexpr (kSwap) {
+                    store_quad(p, acc_col0 + rr, acc_row0 + cc, acc[u]);   // row = m, cols = n
+                } else {
+                    store_quad(p, acc_row0 + rr, acc_col0 + cc, acc[u]);
+                }
             }
         }
         cluster_sync();
@@ -789,6 +817,362 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     if (warp == 5) {
         tc_fence_after_sync();
         tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+// ================================================ stream-K persistent kernel ====
+//
+// One CTA per SM over (tile, 64-deep K block) work. The first T - n_sk tiles
+// are processed whole, in waves (CTA g takes tiles g, g + G, ...), which keeps
+// concurrently processed tiles adjacent in raster order (L2 reuse). The last
+// n_sk tiles' K blocks are cut into G equal contiguous ranges, one per CTA,
+// so every SM ends at the same time whatever T is (n_sk = 0: whole tiles
+// only). The host picks n_sk so that each range spans at least one tile:
+// a tile is then shared by at most two CTAs. The CTA owning a split tile's
+// last K block finishes it: it adds the FP32 partial that lower-numbered CTAs
+// left in their workspace slots (fixed order - deterministic) and stores C.
+// Each CTA processes its range backwards, so the partial it owes is computed
+// first and the tile it finishes last. Finishers only wait for lower-numbered
+// CTAs; the launch is cooperative, so all CTAs are resident. A slot's flag
+// holds the launch's epoch while its partial is valid; the finisher resets it
+// to 0 after use (safe under CUDA-graph replay). All waits are bounded.
+//
+// Partial slots are stored as float4 columns-major-by-quad ([quad][row]),
+// so that both the producer's stores and the finisher's reads are
+// coalesced; the finisher pulls a slot into the (then idle) stage buffers
+// with one bulk copy.
+//
+// kSwap as in hgemm_tile_kernel (accumulator rows = output columns).
+
+struct Seg {
+    int tile, kb0, kb1;   // K blocks [kb0, kb1) of tile
+};
+
+// Segments of one CTA, in processing order. Every role iterates identically.
+struct SegIter {
+    long long start, pe;     // stream-K part: remaining range [start, pe) of K-block positions
+    int next_tile, G, T_dp, KB;
+    __device__ SegIter(int g, int G_, int T, int KB_, int n_sk) : G(G_), T_dp(T - n_sk), KB(KB_) {
+        const long long base = static_cast<long long>(T - n_sk) * KB_;
+        const long long W = static_cast<long long>(n_sk) * KB_;
+        start = base + W * g / G_;
+        pe = base + W * (g + 1) / G_;
+        next_tile = g;
+    }
+    __device__ bool next(Seg& s) {
+        if (next_tile < T_dp) {
+            s.tile = next_tile;
+            s.kb0 = 0;
+            s.kb1 = KB;
+            next_tile += G;
+            return true;
+        }
+        if (pe <= start) return false;
+        const int tile = static_cast<int>((pe - 1) / KB);
+        const long long t0 = static_cast<long long>(tile) * KB;
+        const long long ps = start > t0 ? start : t0;
+        s.tile = tile;
+        s.kb0 = static_cast<int>(ps - t0);
+        s.kb1 = static_cast<int>(pe - t0);
+        pe = ps;
+        return true;
+    }
+};
+
+// CTA whose stream-K range contains K-block position `pos` (relative to the
+// start of the stream-K part, W positions in total).
+__device__ __forceinline__ int sk_owner(long long pos, int G, long long W) {
+    int g = static_cast<int>(pos * G / W);
+    while (g + 1 < G && W * (g + 1) / G <= pos) ++g;
+    while (g > 0 && W * g / G > pos) --g;
+    return g;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <int kBNm, bool kSwap, int kStages>
+struct StreamKCfg {
+    static constexpr int kKRows = kSwap ? kBNm : kMmaM;
+    static constexpr int kMNCols = kSwap ? kMmaM : kBNm;
+    static constexpr uint32_t kKBytes = kKRows * 128u;
+    static constexpr uint32_t kMNBytes = kMNCols * 128u;
+    static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kBarBytes = 256;
+    static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
+    static constexpr uint32_t kAccCols = tmem_cols_for(kBNm);       // one accumulator
+    static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kAccCols);
+    static constexpr uint32_t kIdesc = make_idesc_f16(kMmaM, kBNm, kSwap, !kSwap);
+    static constexpr int kChunk = kBNm >= 32 ? 32 : 16;
+    static constexpr uint32_t kSlotBytes = static_cast<uint32_t>(kMmaM) * kBNm * 4u;
+    static_assert(kKRows % 8 == 0 && kMNCols % 64 == 0, "tile shape");
+    static_assert(kBNm % 16 == 0 && kBNm >= 16 && kBNm <= 256, "UMMA N for M=128");
+    static_assert(2 * kStages + 9 <= 31, "barrier area");
+    static_assert(kSlotBytes <= kDataBytes, "a partial slot must fit the stage buffers");
+    static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+template <int kBNm, bool kSwap, int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_mn,
+                     const GemmParams p) {
+    using Cfg = StreamKCfg<kBNm, kSwap, kStages>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align_1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;      // [2]
+    uint64_t* tempty = tfull + 2;           // [2]
+    uint64_t* drain = tempty + 2;
+    uint64_t* published = drain + 1;        // 128 epilogue threads wrote the partial
+    uint64_t* consumed = published + 1;     // 128 epilogue threads read the partial
+    uint64_t* landed = consumed + 1;        // a producer's slot arrived in shared memory
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(landed + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_index();
+    const uint32_t lane = threadIdx.x & 31u;
+
+    if (warp == 4 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1u);
+            mbar_init(&empty[s], 1u);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1u);
+            mbar_init(&tempty[i], 128u);
+        }
+        mbar_init(drain, 1u);
+        mbar_init(published, 128u);   // a CTA produces <= 1 partial and finishes <= 1 tile,
+        mbar_init(consumed, 128u);    // so these are used at most once per launch ...
+        mbar_init(landed, 1u);        // ... and this once per producer slot read
+        *abort_flag = 0;
+        mbar_init_fence();
+        tma_prefetch_map(&tm_k);
+        tma_prefetch_map(&tm_mn);
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+    // Accumulator tiles: rows = M (N when swapped) in 128s, cols = kBNm wide.
+    const int rows_total = kSwap ? p.n : p.m;
+    const int cols_total = kSwap ? p.m : p.n;
+    const int tiles_r = (rows_total + kMmaM - 1) / kMmaM;
+    const int tiles_c = (cols_total + kBNm - 1) / kBNm;
+    const int T = tiles_r * tiles_c;
+    const int KB = (p.k + kBlockK - 1) / kBlockK;
+    const int G = gridDim.x;
+    const int g = blockIdx.x;
+    const int n_sk = p.streamk;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            SegIter it(g, G, T, KB, n_sk);
+            Seg sg;
+            while (ok && it.next(sg)) {
+                int tr, tc;
+                tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc);
+                const int k_rows0 = kSwap ? tc * kBNm : tr * kMmaM;
+                const int mn_cols0 = kSwap ? tr * kMmaM : tc * kBNm;
+                for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
+                    uint8_t* s_k = smem + stage * Cfg::kStageBytes;
+                    uint8_t* s_mn = s_k + Cfg::kKBytes;
+                    const uint32_t extra = (p.inject && issued == 0) ? 16u : 0u;
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes + extra);
+                    tma_load_2d(s_k, &tm_k, &full[stage], kb * kBlockK, k_rows0);
+#pragma unroll
+                    for (int j = 0; j < Cfg::kMNCols / 64; ++j)
+                        tma_load_2d(s_mn + j * kChunkBytes, &tm_mn, &full[stage], mn_cols0 + 64 * j,
+                                    kb * kBlockK);
+                    ++issued;
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (!ok || *abort_flag) drain_tma<kStages>(full, issued);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, iter = 0;
+            bool ok = true;
+            SegIter it(g, G, T, KB, n_sk);
+            Seg sg;
+            while (ok && it.next(sg)) {
+                const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, wc)) { ok = false; break; }
+                tc_fence_after_sync();
+                const uint32_t d = tmem_base + acc * Cfg::kAccCols;
+                for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
+                    tc_fence_after_sync();
+                    const uint32_t s_k = smem_addr(smem + stage * Cfg::kStageBytes);
+                    const uint32_t s_mn = s_k + Cfg::kKBytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 16; ++kk) {
+                        const uint64_t dk = kmaj_desc(s_k, kk);
+                        const uint64_t dmn = mnmaj_desc(s_mn, kk);
+                        tc_mma_f16(d, kSwap ? dmn : dk, kSwap ? dk : dmn, Cfg::kIdesc,
+                                   (kb > sg.kb0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit(&tfull[acc]);
+                ++iter;
+            }
+            if (!ok) {
+                tc_commit(drain);
+                mbar_wait_drain(drain, 0, kDrainLimitNs);
+            }
+        }
+    } else {
+        const uint32_t t_lane = (warp * 32u) << 16;
+        const int r = warp * 32 + lane;                 // accumulator row (TMEM lane)
+        const long long W_sk = static_cast<long long>(n_sk) * KB;
+        const long long base_sk = static_cast<long long>(T - n_sk) * KB;
+        uint32_t iter = 0;
+        SegIter it(g, G, T, KB, n_sk);
+        Seg sg;
+        while (it.next(sg)) {
+            const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+            ++iter;
+            if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wc))) break;
+            tc_fence_after_sync();
+            int tr, tc;
+            tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc);
+            const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kAccCols;
+            const bool produce = sg.kb1 < KB;                 // partial owed to a later CTA
+            const bool finish = !produce && sg.kb0 > 0;       // adds earlier CTAs' partials
+            int p_lo = g;
+            if (finish) {
+                p_lo = sk_owner(static_cast<long long>(sg.tile) * KB - base_sk, G, W_sk);
+                // Wait (bounded) until every earlier CTA's partial of this tile is published.
+                bool ready = true;
+                for (int q = p_lo; q < g && ready; ++q) {
+                    const uint64_t t0 = global_timer_ns();
+                    while (ld_acquire_u64(p.flags + q) != p.epoch) {
+                        if (*abort_flag || global_timer_ns() - t0 > p.timeout_ns) {
+                            raise_abort(wc, kStatusPipelineTimeout);
+                            ready = false;
+                            break;
+                        }
+                    }
+                }
+                if (!__all_sync(0xffffffffu, ready)) {
+                    tc_fence_before_sync();
+                    mbar_arrive(&tempty[acc]);
+                    break;
+                }
+            }
+            // The finisher segment is this CTA's last: the stage buffers are idle
+            // (its MMAs completed). With a single producer (what the host plans)
+            // its slot is pulled there with bulk copies; with several, slots
+            // are read from global memory. Either way the sum is
+            // (slot p_lo + ... + slot g-1) + own, in that order.
+            const float4* staged = reinterpret_cast<const float4*>(smem);
+            const float4* slots = reinterpret_cast<const float4*>(p.partials);
+            constexpr size_t kSlotQuads = Cfg::kSlotBytes / 16;
+            float4* my_slot = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(g) * kSlotQuads;
+            const bool one_producer = finish && p_lo == g - 1;
+            bool ok_tile = true;
+            if (one_producer) {
+                if (r == 0) {
+                    mbar_arrive_expect_tx(landed, Cfg::kSlotBytes);
+                    const uint8_t* src = reinterpret_cast<const uint8_t*>(slots + static_cast<size_t>(p_lo) * kSlotQuads);
+                    for (uint32_t off = 0; off < Cfg::kSlotBytes; off += 32768u) {
+                        const uint32_t n = Cfg::kSlotBytes - off < 32768u ? Cfg::kSlotBytes - off : 32768u;
+                        bulk_load(smem + off, src + off, n, landed);
+                    }
+                }
+                ok_tile = __all_sync(0xffffffffu, mbar_wait(landed, 0, wc));
+            }
+            if (ok_tile) {
+#pragma unroll 1
+                for (int c = 0; c < kBNm; c += Cfg::kChunk) {
+                    uint32_t v[Cfg::kChunk];
+                    if constexpr (Cfg::kChunk == 32) {
+                        tmem_ld_32x32b_x32(t_acc + c, v);
+                    } else {
+                        tmem_ld_32x32b_x16(t_acc + c, v);
+                    }
+                    tmem_wait_ld();
+                    if (produce) {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kChunk; j += 4)
+                            my_slot[((c + j) / 4) * kMmaM + r] = make_float4(
+                                __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                __uint_as_float(v[j + 3]));
+                        continue;
+                    }
+                    if (finish) {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kChunk; j += 4) {
+                            const size_t qi = static_cast<size_t>((c + j) / 4) * kMmaM + r;
+                            float4 sum;
+                            if (one_producer) {
+                                sum = staged[qi];
+                            } else {
+                                sum = __ldcg(slots + static_cast<size_t>(p_lo) * kSlotQuads + qi);
+                                for (int q = p_lo + 1; q < g; ++q) {
+                                    const float4 x = __ldcg(slots + static_cast<size_t>(q) * kSlotQuads + qi);
+                                    sum.x += x.x; sum.y += x.y; sum.z += x.z; sum.w += x.w;
+                                }
+                            }
+                            v[j] = __float_as_uint(sum.x + __uint_as_float(v[j]));
+                            v[j + 1] = __float_as_uint(sum.y + __uint_as_float(v[j + 1]));
+                            v[j + 2] = __float_as_uint(sum.z + __uint_as_float(v[j + 2]));
+                            v[j + 3] = __float_as_uint(sum.w + __uint_as_float(v[j + 3]));
+                        }
+                    }
+                    if constexpr (kSwap) {
+                        store_col_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
+                    } else {
+                        store_row_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
+                    }
+                }
+            }
+            tc_fence_before_sync();
+            mbar_arrive(&tempty[acc]);
+            if (!ok_tile) break;
+            if (produce) {
+                // Publish this CTA's partial: each thread fences its stores at
+                // GPU scope and arrives; thread 0 waits (bounded) for all 128
+                // and then release-stores the flag.
+                __threadfence();
+                mbar_arrive(published);
+                if (r == 0 && mbar_wait(published, 0, wc)) st_release_u64(p.flags + g, p.epoch);
+            } else if (finish) {
+                // Once all 128 threads have read the partial, reset its flag so
+                // that a replay of this launch waits for a fresh one.
+                mbar_arrive(consumed);
+                if (r == 0 && mbar_wait(consumed, 0, wc))
+                    for (int q = p_lo; q < g; ++q) p.flags[q] = 0ull;
+            }
+        }
+    }
+
+    __syncwarp();
+    tc_fence_before_sync();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after_sync();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
     }
 }
 

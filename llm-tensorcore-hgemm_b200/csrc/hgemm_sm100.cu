@@ -13,6 +13,7 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <random>
 #include <unordered_map>
 
 #include "hgemm_kernels.cuh"
@@ -36,6 +37,8 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_generic_128x128",
     "tc_pair_256x256",
     "tc_splitk_128x256",
+    "tc_streamk_128x256",
+    "tc_streamk_swapab",
 };
 
 // ------------------------------------------------------ device properties --
@@ -176,6 +179,11 @@ int prepare_kernel(KernelEntry& k, int dev) {
     KernelEntry {                                                                          \
         reinterpret_cast<const void*>(&hgemm_pair_kernel<ST>), PairCfg<ST>::kSmemBytes     \
     }
+#define HG_STREAMK(BN, SWAP, ST)                                                          \
+    KernelEntry {                                                                          \
+        reinterpret_cast<const void*>(&hgemm_streamk_kernel<BN, SWAP, ST>),                \
+            StreamKCfg<BN, SWAP, ST>::kSmemBytes                                           \
+    }
 #define HG_PERSIST(BN, ST)                                                                \
     KernelEntry {                                                                          \
         reinterpret_cast<const void*>(&hgemm_persistent_kernel<BN, ST>),                   \
@@ -183,6 +191,11 @@ int prepare_kernel(KernelEntry& k, int dev) {
     }
 
 KernelEntry g_pair_256 = HG_PAIR(6);
+KernelEntry g_sk_256 = HG_STREAMK(256, false, 4);
+KernelEntry g_sk_swap_16 = HG_STREAMK(16, true, 10);
+KernelEntry g_sk_swap_32 = HG_STREAMK(32, true, 9);
+KernelEntry g_sk_swap_64 = HG_STREAMK(64, true, 8);
+KernelEntry g_sk_swap_128 = HG_STREAMK(128, true, 6);
 KernelEntry g_persist_256 = HG_PERSIST(256, 4);
 KernelEntry g_persist_128 = HG_PERSIST(128, 6);
 KernelEntry g_splitk_128 = HG_TILE(128, false, true, 6);
@@ -232,6 +245,63 @@ int check_args(const HgemmSm100Args* a) {
     if (a->config < 0 || a->config >= HGEMM_SM100_CFG_COUNT) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
     if (a->split_k < 0 || a->split_k > kMaxSplit) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
     return HGEMM_SM100_OK;
+}
+
+// Stream-K configurations: tile geometry, grid and workspace of one launch.
+struct StreamKPlan {
+    KernelEntry* k = nullptr;
+    int bnm = 0;
+    bool swap = false;
+    int64_t tiles = 0, kb = 0;
+    int grid = 0;
+    int streamk = 0;         // tiles split into K ranges (the last ones); 0 = none
+    size_t slot_bytes = 0;   // one FP32 partial tile
+    size_t bytes = 0;        // partial slots + flags
+};
+
+bool is_streamk(int32_t cfg) {
+    return cfg == HGEMM_SM100_CFG_STREAMK_128x256 || cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB;
+}
+
+StreamKPlan plan_streamk(int32_t cfg, int64_t m, int64_t n, int64_t k, int sms) {
+    StreamKPlan sp;
+    if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB) {
+        sp.swap = true;
+        if (m <= 16) { sp.bnm = 16; sp.k = &g_sk_swap_16; }
+        else if (m <= 32) { sp.bnm = 32; sp.k = &g_sk_swap_32; }
+        else if (m <= 64) { sp.bnm = 64; sp.k = &g_sk_swap_64; }
+        else { sp.bnm = 128; sp.k = &g_sk_swap_128; }
+        sp.tiles = cdiv(n, 128) * cdiv(m, sp.bnm);
+    } else {
+        sp.bnm = 256;
+        sp.k = &g_sk_256;
+        sp.tiles = cdiv(m, 128) * cdiv(n, 256);
+    }
+    sp.kb = cdiv(k, kBlockK);
+    // Whole tiles in waves; when the last wave is partial, the last
+    // (remainder + one full wave) tiles are split into equal K ranges, each
+    // spanning at least one tile (so a split tile has exactly one producer).
+    // With fewer tiles than SMs the ranges would be shorter than a tile:
+    // whole tiles only (the split-K configurations cover that regime).
+    const int64_t rem = sp.tiles % sms;
+    sp.streamk = (sp.tiles >= sms && rem != 0) ? static_cast<int>(rem + sms) : 0;
+    sp.grid = static_cast<int>(sp.tiles < sms ? sp.tiles : sms);
+    sp.slot_bytes = static_cast<size_t>(128) * sp.bnm * 4;
+    sp.bytes = sp.streamk ? static_cast<size_t>(sp.grid) * (sp.slot_bytes + 8) + 512 : 0;
+    return sp;
+}
+
+std::atomic<uint64_t> g_epoch_counter{0};
+
+// A value no earlier launch of this process used (and, with the random base,
+// none of another process): stale flags in a reused workspace never match.
+uint64_t next_epoch() {
+    static const uint64_t base = [] {
+        std::random_device rd;
+        return (static_cast<uint64_t>(rd()) << 32) ^ static_cast<uint64_t>(rd()) ^ 0x9E3779B97F4A7C15ull;
+    }();
+    uint64_t e = base + 0xD1B54A32D192ED03ull * (g_epoch_counter.fetch_add(1) + 1);
+    return e == 0 ? 1 : e;
 }
 
 // Operand staging: TMA needs 16-byte-aligned bases and row pitches that are
@@ -285,21 +355,39 @@ bool staging_usable(const HgemmSm100Args& a, const Staging& st) {
            reinterpret_cast<uintptr_t>(a.workspace) % kStageAlign == 0;
 }
 
-int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, int32_t* split_out) {
+// Configuration and K split for `a`. With assume_workspace the caller is
+// taken to provide every workspace the result needs (used to size it);
+// otherwise the workspace in `a` decides whether staging and stream-K apply.
+int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_workspace, int32_t* cfg_out,
+                int32_t* split_out) {
     int32_t cfg = a.config;
     const int64_t nkb = cdiv(a.k, kBlockK);
     const int sms = dev.sms > 0 ? dev.sms : 148;
     const Staging st = plan_staging(a);
-    const bool ab_ready = !(st.a || st.b) || staging_usable(a, st);
+    const bool ab_ready = !(st.a || st.b) || assume_workspace || staging_usable(a, st);
     if (!ab_ready) {
         cfg = HGEMM_SM100_CFG_GENERIC_128x128;
     } else if (cfg == HGEMM_SM100_CFG_AUTO) {
-        const int64_t tiles_256 = cdiv(a.m, 128) * cdiv(a.n, 256);
-        if (a.m <= 256) cfg = HGEMM_SM100_CFG_SWAPAB;
-        else if (4 * tiles_256 >= 3 * sms) cfg = HGEMM_SM100_CFG_PERSISTENT_128x256;
-        else cfg = HGEMM_SM100_CFG_SPLITK_128x256;
+        // At least one tile per SM: persistent waves (+ a stream-K split tail).
+        // Fewer tiles than SMs: one tile per CTA, K split across a cluster.
+        if (a.m <= 128) {
+            const int64_t tiles = cdiv(a.n, 128);
+            cfg = tiles >= sms ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_SWAPAB;
+        } else {
+            const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, 256);
+            cfg = tiles >= sms ? HGEMM_SM100_CFG_STREAMK_128x256 : HGEMM_SM100_CFG_SPLITK_128x256;
+        }
     }
     if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x256;
+    if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB && a.m > 128) cfg = HGEMM_SM100_CFG_STREAMK_128x256;
+    if (is_streamk(cfg) && !assume_workspace) {
+        const StreamKPlan sp = plan_streamk(cfg, a.m, a.n, a.k, sms);
+        const size_t need = align_up(st.total, kStageAlign) + sp.bytes;
+        const size_t have = a.workspace != nullptr ? a.workspace_bytes : 0;
+        if (sp.bytes > 0 && have < need)
+            cfg = cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB ? HGEMM_SM100_CFG_SWAPAB
+                                                        : HGEMM_SM100_CFG_PERSISTENT_128x256;
+    }
 
     int32_t split = 1;
     if (cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_SPLITK_128x256 ||
@@ -324,21 +412,35 @@ int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, in
     return HGEMM_SM100_OK;
 }
 
+int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, int32_t* split_out) {
+    return resolve_cfg(a, dev, false, cfg_out, split_out);
+}
+
 int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0, const CUtensorMap& m1,
-           const GemmParams& p, cudaStream_t stream, int cluster_x = 1) {
+           const GemmParams& p, cudaStream_t stream, int cluster_x = 1, bool cooperative = false) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
     if (cluster_z > 1 || cluster_x > 1) {
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = static_cast<unsigned>(cluster_x);
-        attr[0].val.clusterDim.y = 1;
-        attr[0].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = static_cast<unsigned>(cluster_z);
+        ++n;
+    }
+    if (cooperative) {
+        // Stream-K finishers wait for other CTAs: all must be resident.
+        attr[n].id = cudaLaunchAttributeCooperative;
+        attr[n].val.cooperative = 1;
+        ++n;
+    }
+    if (n > 0) {
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = n;
     }
     const KernelFn fn = reinterpret_cast<KernelFn>(const_cast<void*>(k.fn));
     const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, m0, m1, p);
@@ -364,7 +466,7 @@ int launch_copy(const __half* src, int64_t ld_src, __half* dst, int64_t ld_dst, 
 // Launches the resolved configuration on operands that TMA can describe
 // (or, for the generic configuration, on any operands).
 int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceInfo& dev, int devid,
-             cudaStream_t stream) {
+             cudaStream_t stream, uint8_t* sk_region) {
     int rc = HGEMM_SM100_OK;
     GemmParams p{};
     p.a = static_cast<const __half*>(a.a);
@@ -435,6 +537,30 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                             static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
             return launch(*sc.k, grid, split, map_k, map_mn, p, stream);
         }
+        case HGEMM_SM100_CFG_STREAMK_128x256:
+        case HGEMM_SM100_CFG_STREAMK_SWAPAB: {
+            const StreamKPlan sp = plan_streamk(cfg, a.m, a.n, a.k, dev.sms);
+            if (sp.swap) {
+                if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(sp.bnm))) !=
+                    HGEMM_SM100_OK)
+                    return rc;
+            } else if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) {
+                return rc;
+            }
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(*sp.k, devid)) != HGEMM_SM100_OK) return rc;
+            p.streamk = sp.streamk;
+            p.group_m = sp.swap ? 1 : 16;
+            if (sp.streamk) {
+                if (sk_region == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+                p.partials = reinterpret_cast<float*>(sk_region);
+                p.flags = reinterpret_cast<unsigned long long*>(sk_region +
+                                                                static_cast<size_t>(sp.grid) * sp.slot_bytes);
+                p.epoch = next_epoch();
+            }
+            return launch(*sp.k, dim3(static_cast<unsigned>(sp.grid), 1, 1), 1, map_k, map_mn, p, stream, 1,
+                          sp.streamk != 0);
+        }
         case HGEMM_SM100_CFG_GENERIC_128x128: {
             if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
@@ -474,13 +600,17 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     rc = resolve(*args, *dev, &cfg, &split);
     if (rc != HGEMM_SM100_OK) return rc;
 
+    // Workspace layout: [staging buffers][stream-K partial slots + flags].
     const Staging st = plan_staging(*args);
-    if (cfg == HGEMM_SM100_CFG_GENERIC_128x128 || !staging_usable(*args, st))
-        return run_core(*args, cfg, split, *dev, devid, stream);
+    const bool staged = cfg != HGEMM_SM100_CFG_GENERIC_128x128 && staging_usable(*args, st);
+    uint8_t* ws = static_cast<uint8_t*>(args->workspace);
+    uint8_t* sk_region = nullptr;
+    if (is_streamk(cfg) && ws != nullptr) sk_region = ws + align_up(staged ? st.total : 0, kStageAlign);
+
+    if (!staged) return run_core(*args, cfg, split, *dev, devid, stream, sk_region);
 
     // Stage, run on the staged operands, copy a staged C back.
     HgemmSm100Args s = *args;
-    uint8_t* ws = static_cast<uint8_t*>(args->workspace);
     if (st.a) {
         __half* dst = reinterpret_cast<__half*>(ws + st.off_a);
         if ((rc = launch_copy(static_cast<const __half*>(args->a), args->lda, dst, st.lda, args->m, args->k,
@@ -503,7 +633,7 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     }
     s.config = cfg;
     s.split_k = split;
-    if ((rc = run_core(s, cfg, split, *dev, devid, stream)) != HGEMM_SM100_OK) return rc;
+    if ((rc = run_core(s, cfg, split, *dev, devid, stream, sk_region)) != HGEMM_SM100_OK) return rc;
     if (st.c)
         return launch_copy(static_cast<const __half*>(s.c), st.ldc, static_cast<__half*>(args->c), args->ldc,
                            args->m, args->n, false, dev->sms, stream);
@@ -512,7 +642,18 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
 
 extern "C" size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args) {
     if (check_args(args) != HGEMM_SM100_OK) return 0;
-    return plan_staging(*args).total;
+    const Staging st = plan_staging(*args);
+    size_t total = st.total;
+    const DeviceInfo* dev = nullptr;
+    if (device_info(&dev) != HGEMM_SM100_OK) return total;
+    int32_t cfg = 0, split = 0;
+    resolve_cfg(*args, *dev, true, &cfg, &split);
+    if (cfg == HGEMM_SM100_CFG_GENERIC_128x128) return 0;
+    if (is_streamk(cfg)) {
+        const StreamKPlan sp = plan_streamk(cfg, args->m, args->n, args->k, dev->sms);
+        if (sp.bytes > 0) total = align_up(total, kStageAlign) + sp.bytes;
+    }
+    return total;
 }
 
 extern "C" int32_t hgemm_sm100_config_from_name(const char* name) {
@@ -529,7 +670,12 @@ extern "C" const char* hgemm_sm100_config_name(int32_t config) {
 
 extern "C" int32_t hgemm_sm100_num_configs(void) { return HGEMM_SM100_CFG_COUNT; }
 
-extern "C" size_t hgemm_sm100_workspace_bytes(int32_t, int64_t, int64_t, int64_t) { return 0; }
+extern "C" size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k) {
+    if (!is_streamk(config) || m <= 0 || n <= 0 || k <= 0) return 0;
+    const DeviceInfo* dev = nullptr;
+    if (device_info(&dev) != HGEMM_SM100_OK) return 0;
+    return plan_streamk(config, m, n, k, dev->sms).bytes;
+}
 
 extern "C" const char* hgemm_sm100_status_string(int status) {
     switch (status) {

@@ -29,6 +29,8 @@ CFG_SWAPAB = 4
 CFG_GENERIC_128x128 = 5
 CFG_PAIR_256x256 = 6
 CFG_SPLITK_128x256 = 7
+CFG_STREAMK_128x256 = 8
+CFG_STREAMK_SWAPAB = 9
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2

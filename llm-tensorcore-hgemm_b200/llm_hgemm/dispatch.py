@@ -36,6 +36,8 @@ CUSTOM_PROVIDERS = (
     "tc_generic_128x128",
     "tc_pair_256x256",
     "tc_splitk_128x256",
+    "tc_streamk_128x256",
+    "tc_streamk_swapab",
 )
 MISALIGNED_PROVIDER = "auto"
 DEFAULT_PROVIDER = "auto"

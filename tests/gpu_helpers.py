@@ -15,6 +15,8 @@ IMPLEMENTATIONS = [
     "tc_generic_128x128",
     "tc_pair_256x256",
     "tc_splitk_128x256",
+    "tc_streamk_128x256",
+    "tc_streamk_swapab",
 ]
 
 

@@ -23,6 +23,8 @@ CONFIG_IDS = {
     "tc_generic_128x128": capi.CFG_GENERIC_128x128,
     "tc_pair_256x256": capi.CFG_PAIR_256x256,
     "tc_splitk_128x256": capi.CFG_SPLITK_128x256,
+    "tc_streamk_128x256": capi.CFG_STREAMK_128x256,
+    "tc_streamk_swapab": capi.CFG_STREAMK_SWAPAB,
 }
 
 
@@ -32,10 +34,15 @@ def _cuda():
 
 
 def run_capi(a, b, out, config, split_k=0, flags=0):
+    """Calls the C ABI with the workspace it asks for (staging, stream-K)."""
     m, k = a.shape
     n = b.shape[1]
     args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
                           config=config, split_k=split_k, flags=flags)
+    need = capi.workspace_size(args)
+    ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
+    if need:
+        args.workspace, args.workspace_bytes = ws.data_ptr(), need
     rc = capi.run(args, torch.cuda.current_stream().cuda_stream)
     assert rc == capi.OK, capi.status_string(rc)
     return out
@@ -169,7 +176,9 @@ def test_staged_ragged_operands(config, shape):
     ws = torch.empty(need, device="cuda", dtype=torch.uint8)
     args.workspace, args.workspace_bytes = ws.data_ptr(), need
     rc, cfg, _ = capi.resolve(args)
-    assert rc == capi.OK and cfg == CONFIG_IDS[config] or config == "tc_swapab"
+    # Swap-AB configurations hand M beyond their range to the 128x256 kernels.
+    remap = {"tc_swapab": capi.CFG_SPLITK_128x256, "tc_streamk_swapab": capi.CFG_STREAMK_128x256}
+    assert rc == capi.OK and cfg in (CONFIG_IDS[config], remap.get(config))
     assert capi.run(args, torch.cuda.current_stream().cuda_stream) == capi.OK
     assert_gate(out, a, b)
     # Without a workspace the same call runs the generic (no-TMA) kernel.

@@ -23,6 +23,8 @@ TMA_CONFIGS = {
     "tc_splitk_128x128": (capi.CFG_SPLITK_128x128, (128, 256, 1024)),
     "tc_splitk_128x256": (capi.CFG_SPLITK_128x256, (128, 512, 1024)),
     "tc_swapab": (capi.CFG_SWAPAB, (16, 512, 1024)),
+    "tc_streamk_128x256": (capi.CFG_STREAMK_128x256, (300, 520, 2056)),
+    "tc_streamk_swapab": (capi.CFG_STREAMK_SWAPAB, (8, 1000, 3000)),
 }
 
 
@@ -41,12 +43,18 @@ def test_injected_stall_times_out_and_context_survives(name):
     args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, config=cfg,
                           flags=capi.FLAG_TEST_INJECT_TX, status_ptr=status.data_ptr(),
                           timeout_ns=50_000_000)
+    need = capi.workspace_size(args)
+    ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
+    if need:
+        args.workspace, args.workspace_bytes = ws.data_ptr(), need
     assert capi.run(args, stream) == capi.OK
     torch.cuda.synchronize()
     assert int(status.item()) == capi.ERR_PIPELINE_TIMEOUT
     # The context is intact: the same configuration now computes correctly.
     good = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
     args_ok = capi.make_args(a.data_ptr(), b.data_ptr(), good.data_ptr(), m, n, k, config=cfg)
+    if need:
+        args_ok.workspace, args_ok.workspace_bytes = ws.data_ptr(), need
     assert capi.run(args_ok, stream) == capi.OK
     assert_gate(good, a, b)
 
