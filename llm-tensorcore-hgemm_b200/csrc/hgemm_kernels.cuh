@@ -59,6 +59,7 @@ struct GemmParams {
     int m, n, k;
     long long lda, ldb, ldc;
     int vec_ok;            // C base 16-byte aligned and ldc % 8 == 0
+    int tma_store;         // persistent/pair kernels: store C tiles with TMA (FP16, vec_ok)
     int out_f32;           // store FP32 instead of FP16 (tensor-parallel partials)
     int group_m;           // persistent kernel: M-tiles per raster group
     int inject;            // test-only: arm the first stage with 16 extra bytes
@@ -148,6 +149,33 @@ __device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col
         if (col + 1 < p.n) c[1] = __float2half_rn(v.y);
         if (col + 2 < p.n) c[2] = __float2half_rn(v.z);
         if (col + 3 < p.n) c[3] = __float2half_rn(v.w);
+    }
+}
+
+// TMA-store epilogue: converts 64 accumulator columns of this warp's 32 rows
+// (lane = row) to FP16 in a 128-byte-swizzled 32 x 64 shared-memory box and
+// lane 0 stores the box with TMA at output (x = col0, y = row0). `buf`
+// alternates between two boxes per warp; before a box is rewritten, the
+// store that read it two boxes ago must have finished reading.
+__device__ __forceinline__ void store_box_tma(const CUtensorMap* map, uint8_t* box, uint32_t lane,
+                                              const uint32_t* v0, const uint32_t* v1, int col0, int row0) {
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t* v = j < 4 ? v0 + 8 * j : v1 + 8 * (j - 4);
+        uint4 q;
+        q.x = pack_half2(v[0], v[1]);
+        q.y = pack_half2(v[2], v[3]);
+        q.z = pack_half2(v[4], v[5]);
+        q.w = pack_half2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(box + lane * 128u + ((static_cast<uint32_t>(j) ^ (lane & 7u)) << 4)) = q;
+    }
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(map, box, col0, row0);
+        bulk_commit_group();
     }
 }
 
@@ -274,7 +302,8 @@ struct TileCfg {
 template <int kBNm, bool kSwap, bool kTma, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_mn,
-                  const GemmParams p) {
+                  const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+    (void)tm_c;
     using Cfg = TileCfg<kBNm, kSwap, kTma, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
@@ -488,7 +517,8 @@ struct PersistCfg {
     static constexpr uint32_t kABytes = kMmaM * 128u;        // 128 x 64 halves
     static constexpr uint32_t kBBytes = kBN * 128u;          // 64 x kBN halves
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kEpiBytes = 4u * 2u * 4096u;   // 4 warps x 2 boxes of 32 x 64 halves
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
     static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kBN);
@@ -512,7 +542,7 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 template <int kBN, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
     using Cfg = PersistCfg<kBN, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
@@ -612,7 +642,8 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
     } else {
         // Epilogue warps 0-3: warp w owns TMEM lanes 32w .. 32w + 31.
         const uint32_t t_lane = (warp * 32u) << 16;
-        uint32_t iter = 0;
+        uint8_t* boxes = smem + kStages * Cfg::kStageBytes + warp * 8192u;
+        uint32_t buf = 0, iter = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++iter) {
             const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wc))) break;
@@ -621,16 +652,30 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
             tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
             const int row = tm * kMmaM + warp * 32 + lane;
             const uint32_t t_acc = tmem_base + t_lane + acc * kBN;
+            if (p.tma_store) {
 #pragma unroll 1
-            for (int c = 0; c < kBN; c += 32) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(t_acc + c, v);
-                tmem_wait_ld();
-                store_row_segment<32>(p, row, tn * kBN + c, v);
+                for (int c = 0; c < kBN; c += 64) {
+                    uint32_t v0[32], v1[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v0);
+                    tmem_ld_32x32b_x32(t_acc + c + 32, v1);
+                    tmem_wait_ld();
+                    store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, tn * kBN + c,
+                                  tm * kMmaM + warp * 32);
+                    buf ^= 1u;
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < kBN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v);
+                    tmem_wait_ld();
+                    store_row_segment<32>(p, row, tn * kBN + c, v);
+                }
             }
             tc_fence_before_sync();
             mbar_arrive(&tempty[acc]);
         }
+        if (p.tma_store && lane == 0) bulk_wait_group_all();
     }
 
     __syncwarp();
@@ -660,7 +705,8 @@ struct PairCfg {
     static constexpr uint32_t kABytes = 128u * 128u;        // 128 rows x 64 halves
     static constexpr uint32_t kBBytes = 128u * 128u;        // 64 k-rows x 128 halves
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kEpiBytes = 4u * 2u * 4096u;   // 4 warps x 2 boxes of 32 x 64 halves
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
     static constexpr uint32_t kTmemCols = 512;              // 2 x 256 FP32 columns
@@ -672,7 +718,7 @@ struct PairCfg {
 template <int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                  const GemmParams p) {
+                  const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
     using Cfg = PairCfg<kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
@@ -786,26 +832,40 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
         const uint32_t t_lane = (warp * 32u) << 16;
         const uint32_t tempty_leader0 = map_to_rank(smem_addr(&tempty[0]), 0);
         const uint32_t tempty_leader1 = map_to_rank(smem_addr(&tempty[1]), 0);
-        uint32_t iter = 0;
+        uint8_t* boxes = smem + kStages * Cfg::kStageBytes + warp * 8192u;
+        uint32_t buf = 0, iter = 0;
         for (int t = pair; t < num_tiles; t += npairs, ++iter) {
             const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tfull[acc], acc_phase, wc))) break;
             tc_fence_after_sync();
             int tm, tn;
             tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-            const int row = tm * Cfg::kTileM + static_cast<int>(rank) * 128 + warp * 32 + lane;
+            const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * 128 + warp * 32;
             const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kTileN;
+            if (p.tma_store) {
 #pragma unroll 1
-            for (int c = 0; c < Cfg::kTileN; c += 32) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(t_acc + c, v);
-                tmem_wait_ld();
-                store_row_segment<32>(p, row, tn * Cfg::kTileN + c, v);
+                for (int c = 0; c < Cfg::kTileN; c += 64) {
+                    uint32_t v0[32], v1[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v0);
+                    tmem_ld_32x32b_x32(t_acc + c + 32, v1);
+                    tmem_wait_ld();
+                    store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, tn * Cfg::kTileN + c, row0);
+                    buf ^= 1u;
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < Cfg::kTileN; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v);
+                    tmem_wait_ld();
+                    store_row_segment<32>(p, row0 + static_cast<int>(lane), tn * Cfg::kTileN + c, v);
+                }
             }
             tc_fence_before_sync();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
         }
+        if (p.tma_store && lane == 0) bulk_wait_group_all();
     }
 
     __syncwarp();
@@ -904,7 +964,8 @@ struct StreamKCfg {
     static constexpr uint32_t kKBytes = kKRows * 128u;
     static constexpr uint32_t kMNBytes = kMNCols * 128u;
     static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
-    static constexpr uint32_t kDataBytes = kStages * kStageBytes;
+    static constexpr uint32_t kEpiBytes = kSwap ? 0u : 4u * 2u * 4096u;   // TMA-store boxes
+    static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
     static constexpr uint32_t kAccCols = tmem_cols_for(kBNm);       // one accumulator
@@ -915,14 +976,15 @@ struct StreamKCfg {
     static_assert(kKRows % 8 == 0 && kMNCols % 64 == 0, "tile shape");
     static_assert(kBNm % 16 == 0 && kBNm >= 16 && kBNm <= 256, "UMMA N for M=128");
     static_assert(2 * kStages + 9 <= 31, "barrier area");
-    static_assert(kSlotBytes <= kDataBytes, "a partial slot must fit the stage buffers");
+    static_assert(kSlotBytes <= kStages * kStageBytes, "a partial slot must fit the stage buffers");
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 template <int kBNm, bool kSwap, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_mn,
-                     const GemmParams p) {
+                     const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+    (void)tm_c;
     using Cfg = StreamKCfg<kBNm, kSwap, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
@@ -1046,7 +1108,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
         const int r = warp * 32 + lane;                 // accumulator row (TMEM lane)
         const long long W_sk = static_cast<long long>(n_sk) * KB;
         const long long base_sk = static_cast<long long>(T - n_sk) * KB;
-        uint32_t iter = 0;
+        uint32_t iter = 0, epi_buf = 0;
         SegIter it(g, G, T, KB, n_sk);
         Seg sg;
         while (it.next(sg)) {
@@ -1102,7 +1164,44 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                 }
                 ok_tile = __all_sync(0xffffffffu, mbar_wait(landed, 0, wc));
             }
-            if (ok_tile) {
+            if (ok_tile && !kSwap && p.tma_store && !produce) {
+                // Whole or finished tile: 64-column boxes through shared memory.
+                uint8_t* boxes = smem + kStages * Cfg::kStageBytes + warp * 8192u;
+#pragma unroll 1
+                for (int c = 0; c < kBNm; c += 64) {
+                    uint32_t v0[32], v1[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v0);
+                    tmem_ld_32x32b_x32(t_acc + c + 32, v1);
+                    tmem_wait_ld();
+                    if (finish) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            uint32_t* v = h ? v1 : v0;
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) {
+                                const size_t qi = static_cast<size_t>((c + 32 * h + j) / 4) * kMmaM + r;
+                                float4 sum;
+                                if (one_producer) {
+                                    sum = staged[qi];
+                                } else {
+                                    sum = __ldcg(slots + static_cast<size_t>(p_lo) * kSlotQuads + qi);
+                                    for (int q = p_lo + 1; q < g; ++q) {
+                                        const float4 x = __ldcg(slots + static_cast<size_t>(q) * kSlotQuads + qi);
+                                        sum.x += x.x; sum.y += x.y; sum.z += x.z; sum.w += x.w;
+                                    }
+                                }
+                                v[j] = __float_as_uint(sum.x + __uint_as_float(v[j]));
+                                v[j + 1] = __float_as_uint(sum.y + __uint_as_float(v[j + 1]));
+                                v[j + 2] = __float_as_uint(sum.z + __uint_as_float(v[j + 2]));
+                                v[j + 3] = __float_as_uint(sum.w + __uint_as_float(v[j + 3]));
+                            }
+                        }
+                    }
+                    store_box_tma(&tm_c, boxes + epi_buf * 4096u, lane, v0, v1, tc * kBNm + c,
+                                  tr * kMmaM + warp * 32);
+                    epi_buf ^= 1u;
+                }
+            } else if (ok_tile) {
 #pragma unroll 1
                 for (int c = 0; c < kBNm; c += Cfg::kChunk) {
                     uint32_t v[Cfg::kChunk];
@@ -1165,6 +1264,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                     for (int q = p_lo; q < g; ++q) p.flags[q] = 0ull;
             }
         }
+        if (!kSwap && p.tma_store && lane == 0) bulk_wait_group_all();
     }
 
     __syncwarp();

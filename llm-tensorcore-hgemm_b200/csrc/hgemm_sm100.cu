@@ -147,7 +147,7 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t oute
 
 // ---------------------------------------------------------------- kernels --
 
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemmParams);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmParams);
 
 struct KernelEntry {
     const void* fn;
@@ -374,8 +374,12 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             const int64_t tiles = cdiv(a.n, 128);
             cfg = tiles >= sms ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_SWAPAB;
         } else {
+            // >= 4 waves: the partial last wave costs little, the plain
+            // persistent kernel runs the waves fastest.
             const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, 256);
-            cfg = tiles >= sms ? HGEMM_SM100_CFG_STREAMK_128x256 : HGEMM_SM100_CFG_SPLITK_128x256;
+            cfg = tiles >= 4 * static_cast<int64_t>(sms) ? HGEMM_SM100_CFG_PERSISTENT_128x256
+                  : tiles >= sms                         ? HGEMM_SM100_CFG_STREAMK_128x256
+                                                         : HGEMM_SM100_CFG_SPLITK_128x256;
         }
     }
     if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x256;
@@ -417,7 +421,8 @@ int resolve(const HgemmSm100Args& a, const DeviceInfo& dev, int32_t* cfg_out, in
 }
 
 int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0, const CUtensorMap& m1,
-           const GemmParams& p, cudaStream_t stream, int cluster_x = 1, bool cooperative = false) {
+           const CUtensorMap& m2, const GemmParams& p, cudaStream_t stream, int cluster_x = 1,
+           bool cooperative = false) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -443,7 +448,7 @@ int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0
         cfg.numAttrs = n;
     }
     const KernelFn fn = reinterpret_cast<KernelFn>(const_cast<void*>(k.fn));
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, m0, m1, p);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, m0, m1, m2, p);
     return e == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
 }
 
@@ -485,9 +490,19 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
     p.status = a.status != nullptr ? a.status : dev.status_word;
     p.timeout_ns = a.timeout_ns != 0 ? a.timeout_ns : kDefaultTimeoutNs;
 
-    CUtensorMap map_k, map_mn;
+    CUtensorMap map_k, map_mn, map_c;
     std::memset(&map_k, 0, sizeof(map_k));
     std::memset(&map_mn, 0, sizeof(map_mn));
+    std::memset(&map_c, 0, sizeof(map_c));
+    // TMA-store epilogue (persistent and pair kernels): FP16 C whose base and
+    // pitch TMA can describe; boxes of 32 rows x 64 columns.
+    auto prepare_store = [&]() -> int {
+        if (!p.vec_ok || p.out_f32) return HGEMM_SM100_OK;
+        const int r = tensor_map(&map_c, a.c, static_cast<uint64_t>(a.n), static_cast<uint64_t>(a.m),
+                                 static_cast<uint64_t>(a.ldc), 64, 32);
+        if (r == HGEMM_SM100_OK) p.tma_store = 1;
+        return r;
+    };
     const uint64_t M = a.m, N = a.n, K = a.k;
 
     switch (cfg) {
@@ -498,20 +513,22 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             const int bn = wide ? 256 : 128;
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
             const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, bn);
             const int64_t grid = tiles < dev.sms ? tiles : dev.sms;
-            return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, p, stream);
+            return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, map_c, p, stream);
         }
         case HGEMM_SM100_CFG_PAIR_256x256: {
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(g_pair_256, devid)) != HGEMM_SM100_OK) return rc;
             const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, 256);
             const int64_t pairs_max = dev.sms / 2;
             const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
             p.group_m = 8;
-            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, p,
+            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, map_c, p,
                           stream, 2);
         }
         case HGEMM_SM100_CFG_SPLITK_128x128:
@@ -524,7 +541,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, bn)),
                             static_cast<unsigned>(split));
-            return launch(k, grid, split, map_k, map_mn, p, stream);
+            return launch(k, grid, split, map_k, map_mn, map_c, p, stream);
         }
         case HGEMM_SM100_CFG_SWAPAB: {
             const SwapChoice sc = swap_choice(a.m);
@@ -535,7 +552,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             if ((rc = prepare_kernel(*sc.k, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
                             static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
-            return launch(*sc.k, grid, split, map_k, map_mn, p, stream);
+            return launch(*sc.k, grid, split, map_k, map_mn, map_c, p, stream);
         }
         case HGEMM_SM100_CFG_STREAMK_128x256:
         case HGEMM_SM100_CFG_STREAMK_SWAPAB: {
@@ -548,6 +565,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                 return rc;
             }
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if (!sp.swap && (rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(*sp.k, devid)) != HGEMM_SM100_OK) return rc;
             p.streamk = sp.streamk;
             p.group_m = sp.swap ? 1 : 16;
@@ -558,14 +576,14 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                                                                 static_cast<size_t>(sp.grid) * sp.slot_bytes);
                 p.epoch = next_epoch();
             }
-            return launch(*sp.k, dim3(static_cast<unsigned>(sp.grid), 1, 1), 1, map_k, map_mn, p, stream, 1,
+            return launch(*sp.k, dim3(static_cast<unsigned>(sp.grid), 1, 1), 1, map_k, map_mn, map_c, p, stream, 1,
                           sp.streamk != 0);
         }
         case HGEMM_SM100_CFG_GENERIC_128x128: {
             if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
                             static_cast<unsigned>(split));
-            return launch(g_generic_128, grid, split, map_k, map_mn, p, stream);
+            return launch(g_generic_128, grid, split, map_k, map_mn, map_c, p, stream);
         }
         default:
             return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
