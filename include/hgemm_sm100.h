@@ -43,7 +43,9 @@ enum {
     HGEMM_SM100_ERR_LAUNCH = 4,            /* CUDA launch / attribute failure   */
     HGEMM_SM100_ERR_PIPELINE_TIMEOUT = 5,  /* a kernel wait ran out (status word)*/
     HGEMM_SM100_ERR_TENSOR_MAP = 6,        /* cuTensorMapEncodeTiled failed     */
-    HGEMM_SM100_ERR_CUDA = 7               /* other CUDA runtime error          */
+    HGEMM_SM100_ERR_CUDA = 7,              /* other CUDA runtime error          */
+    HGEMM_SM100_ERR_SCRATCH_LIMIT = 8      /* needs more scratch than the static
+                                              buffer of hgemm_sm100_run_static_scratch */
 };
 
 /* Kernel configurations. Every name is also accepted by
@@ -128,6 +130,35 @@ size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t
  * launches nothing. The stream-K part keeps no state between calls: any
  * workspace of this size works, whatever it contains. */
 size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
+
+/* Runs C = A @ B like hgemm_sm100_run, but takes no workspace and allocates
+ * nothing: the scratch that the stream-K kernels need (one FP32 partial-tile
+ * slot and one flag per CTA) comes from a static device buffer of
+ * HGEMM_SM100_STATIC_SCRATCH_BYTES inside this library, which every GPU that
+ * loads the library holds until the process exits.
+ * No counterpart in the reference. It exists for callers that cannot
+ * allocate device memory when they call a GEMM: a plugin or FFI host handed
+ * only input/output pointers and a stream, a runtime that plans all of its
+ * memory ahead of time, or code that must not call cudaMalloc (which can
+ * synchronise the device) on its hot path.
+ * - config: HGEMM_SM100_CFG_AUTO (stream-K; swap-AB for m <= 128) or one of
+ *   the two stream-K configurations; anything else -> ERR_UNKNOWN_CONFIG.
+ * - A and B must satisfy the TMA rules (16-byte-aligned bases, lda and ldb
+ *   multiples of 8); otherwise ERR_INVALID_ARGUMENT (staging would need
+ *   scratch of the operands' size).
+ * - A problem whose scratch exceeds the static buffer is rejected with
+ *   HGEMM_SM100_ERR_SCRATCH_LIMIT and nothing is launched (the swap-AB
+ *   configuration, m <= 128, always fits; a 128x256 stream-K split tail does
+ *   not on a 148-SM GPU).
+ * - The first call on a device looks up the buffer's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture.
+ * - Every call shares the one buffer and it keeps the last call's contents;
+ *   nothing in it needs clearing (each launch's flags carry a fresh value that
+ *   stale contents never equal). Calls that overlap on the GPU (for example
+ *   on two streams) race on it: serialise them. */
+#define HGEMM_SM100_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
+int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* stream);
 
 /* Human-readable text of a status code. */
 const char* hgemm_sm100_status_string(int status);

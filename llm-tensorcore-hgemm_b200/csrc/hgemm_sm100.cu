@@ -705,6 +705,8 @@ extern "C" const char* hgemm_sm100_status_string(int status) {
         case HGEMM_SM100_ERR_PIPELINE_TIMEOUT: return "hgemm: pipeline timeout";
         case HGEMM_SM100_ERR_TENSOR_MAP: return "TMA descriptor encoding failed";
         case HGEMM_SM100_ERR_CUDA: return "CUDA runtime error";
+        case HGEMM_SM100_ERR_SCRATCH_LIMIT:
+            return "problem needs more scratch than the static buffer (HGEMM_SM100_STATIC_SCRATCH_BYTES)";
         default: return "unknown status";
     }
 }
@@ -721,4 +723,58 @@ extern "C" int hgemm_sm100_read_status(int32_t* value, int clear) {
     *value = v;
     if (clear && cudaMemset(dev->status_word, 0, sizeof(int)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
     return HGEMM_SM100_OK;
+}
+
+// ================================================ static-scratch entry point ==
+//
+// For callers that cannot allocate device memory at call time: the stream-K
+// scratch lives in this file-scope device array instead of a caller workspace.
+// In host code `g_static_scratch` only names the symbol (it is not a device
+// address); its device address is looked up once per device below and passed
+// to the kernels like any workspace pointer.
+namespace {
+
+static __device__ __align__(256) unsigned char g_static_scratch[HGEMM_SM100_STATIC_SCRATCH_BYTES];
+
+uint8_t* g_static_scratch_ptr[kMaxDevices];
+int g_static_scratch_rc[kMaxDevices];
+std::once_flag g_static_scratch_once[kMaxDevices];
+
+// Device address of the static scratch on the current device (set up on the
+// first call for that device, with it current).
+int static_scratch(int dev, uint8_t** out) {
+    std::call_once(g_static_scratch_once[dev], [dev] {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        g_static_scratch_ptr[dev] = static_cast<uint8_t*>(ptr);
+        g_static_scratch_rc[dev] = (e == cudaSuccess && ptr != nullptr) ? HGEMM_SM100_OK : HGEMM_SM100_ERR_CUDA;
+    });
+    *out = g_static_scratch_ptr[dev];
+    return g_static_scratch_rc[dev];
+}
+
+}  // namespace
+
+extern "C" int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* stream_ptr) {
+    int rc = check_args(args);
+    if (rc != HGEMM_SM100_OK) return rc;
+    const DeviceInfo* dev = nullptr;
+    rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    int devid = 0;
+    if (cudaGetDevice(&devid) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    if (!fp16_tma_ok(args->a, args->lda) || !fp16_tma_ok(args->b, args->ldb))
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+
+    int32_t cfg = args->config;
+    if (cfg == HGEMM_SM100_CFG_AUTO)
+        cfg = args->m <= 128 ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_STREAMK_128x256;
+    if (!is_streamk(cfg)) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB && args->m > 128) cfg = HGEMM_SM100_CFG_STREAMK_128x256;
+
+    const StreamKPlan sp = plan_streamk(cfg, args->m, args->n, args->k, dev->sms);
+    if (sp.bytes > HGEMM_SM100_STATIC_SCRATCH_BYTES) return HGEMM_SM100_ERR_SCRATCH_LIMIT;
+    uint8_t* scratch = nullptr;
+    if (sp.bytes > 0 && (rc = static_scratch(devid, &scratch)) != HGEMM_SM100_OK) return rc;
+    return run_core(*args, cfg, 1, *dev, devid, static_cast<cudaStream_t>(stream_ptr), scratch);
 }

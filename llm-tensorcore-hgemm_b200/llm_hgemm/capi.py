@@ -20,6 +20,8 @@ ERR_LAUNCH = 4
 ERR_PIPELINE_TIMEOUT = 5
 ERR_TENSOR_MAP = 6
 ERR_CUDA = 7
+ERR_SCRATCH_LIMIT = 8
+STATIC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 CFG_AUTO = 0
 CFG_PERSISTENT_128x256 = 1
@@ -79,6 +81,8 @@ def load() -> ctypes.CDLL:
         lib.hgemm_sm100_workspace_bytes.argtypes = [ctypes.c_int32, ctypes.c_int64,
                                                     ctypes.c_int64, ctypes.c_int64]
         lib.hgemm_sm100_workspace_bytes.restype = ctypes.c_size_t
+        lib.hgemm_sm100_run_static_scratch.argtypes = [ctypes.POINTER(HgemmSm100Args), ctypes.c_void_p]
+        lib.hgemm_sm100_run_static_scratch.restype = ctypes.c_int
         lib.hgemm_sm100_workspace_size.argtypes = [ctypes.POINTER(HgemmSm100Args)]
         lib.hgemm_sm100_workspace_size.restype = ctypes.c_size_t
         lib.hgemm_sm100_status_string.argtypes = [ctypes.c_int]
@@ -102,6 +106,11 @@ def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
 
 def run(args: HgemmSm100Args, stream: int = 0) -> int:
     return load().hgemm_sm100_run(ctypes.byref(args), ctypes.c_void_p(stream))
+
+
+def run_static_scratch(args: HgemmSm100Args, stream: int = 0) -> int:
+    """hgemm_sm100_run_static_scratch: no workspace, nothing allocated."""
+    return load().hgemm_sm100_run_static_scratch(ctypes.byref(args), ctypes.c_void_p(stream))
 
 
 def resolve(args: HgemmSm100Args) -> tuple[int, int, int]:
