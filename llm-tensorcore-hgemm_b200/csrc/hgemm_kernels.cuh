@@ -82,9 +82,15 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
     if (row >= p.m) return;
     if (p.out_f32) {
         float* crow = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc;
+        if (p.vec_ok && col0 + kCnt <= p.n) {
 #pragma unroll
-        for (int i = 0; i < kCnt; ++i)
-            if (col0 + i < p.n) crow[col0 + i] = __uint_as_float(v[i]);
+            for (int i = 0; i < kCnt; i += 4)
+                *reinterpret_cast<uint4*>(crow + col0 + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < kCnt; ++i)
+                if (col0 + i < p.n) crow[col0 + i] = __uint_as_float(v[i]);
+        }
         return;
     }
     __half* crow = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc;

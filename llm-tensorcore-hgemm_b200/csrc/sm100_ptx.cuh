@@ -5,8 +5,8 @@
 //
 // These replace the SM80 wrappers the reference kernels are built on
 // (ldmatrix / mma.sync in csrc/common/layout.cuh:35-88 and cp.async in
-// csrc/common/async_copy.cuh:14-54 of the reference). Nothing here uses TMA
-// multicast: every CTA loads its own operand tiles.
+// csrc/common/async_copy.cuh:14-54 of the reference). Every TMA load here
+// brings one CTA's own operand tile into that CTA's shared memory.
 #pragma once
 
 #include <cuda.h>
@@ -341,7 +341,7 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
 // 2-D tiled TMA load into this CTA's shared memory whose transaction bytes
 // complete on `bar`, an mbarrier of either CTA of the pair (shared::cluster
 // address). Used so that both CTAs' tiles complete on the MMA CTA's barrier.
-// Plain (not multicast) load of this CTA's own tile.
+// Only this CTA's own tile is written.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar,
                                                  int32_t x, int32_t y) {
     asm volatile(
