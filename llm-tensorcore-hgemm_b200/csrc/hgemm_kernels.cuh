@@ -285,12 +285,20 @@ struct TileCfg {
     static constexpr uint32_t kKBytes = kKRows * 128u;
     static constexpr uint32_t kMNBytes = kMNCols * 128u;
     static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
-    // Split-K partial buffer (FP32), laid out so the output's contiguous
-    // dimension is contiguous: [row][col + 4 pad] or, swapped, [m][n].
-    static constexpr uint32_t kRedStride = kSwap ? kMmaM : (kBNm + 4);
-    static constexpr uint32_t kRedRows = kSwap ? kBNm : kMmaM;
-    static constexpr uint32_t kRedBytes = kRedRows * kRedStride * 4u;
-    static constexpr uint32_t kDataBytes = cmax(kStages * kStageBytes, kRedBytes);
+    // Split-K receive buffer (FP32): accumulator rows are divided among the
+    // CTAs of the cluster in whole quads of 4 rows (rank r owns rows from
+    // 4 * (r * 32 / split)); CTA o receives, from every rank s, the rows it
+    // owns: [s][local row][kBNm + 4] or, swapped, [s][col][local row] (the
+    // output's contiguous dimension contiguous, quads 16-byte aligned). Rows
+    // per rank <= 4 * ceil(32 / split); over split 2..16,
+    // split * 4 * ceil(32 / split) <= 180. Small swapped tiles get a buffer of
+    // their own (no overlap with the stage ring); the others reuse the ring
+    // once every CTA's MMAs are done.
+    static constexpr bool kRecvOwn = kSwap && kBNm <= 32;
+    static constexpr uint32_t kRecvBytes = kSwap ? 180u * kBNm * 4u : 180u * (kBNm + 4) * 4u;
+    static constexpr uint32_t kRecvOff = kRecvOwn ? kStages * kStageBytes : 0u;
+    static constexpr uint32_t kDataBytes =
+        kRecvOwn ? kStages * kStageBytes + kRecvBytes : cmax(kStages * kStageBytes, kRecvBytes);
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
     static constexpr uint32_t kTmemCols = tmem_cols_for(kBNm);
@@ -421,15 +429,31 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     __syncwarp();
 
     // --------------------------------------------------------- epilogue --
+    // Without a split the accumulator goes straight to C. With a K split,
+    // every CTA pushes each accumulator row into the receive buffer of the CTA
+    // that owns the row (remote shared-memory stores, no waiting), one cluster
+    // barrier makes them visible, and each CTA sums its rows over ranks
+    // 0..split-1 in order (deterministic) and stores them.
     const bool split_k = split > 1;
+    const uint32_t rank = cluster_ctarank();
+    const int nrows_max = 4 * ((32 + split - 1) / split);   // rows owned per rank, bound
+    const int sw_stride = nrows_max;                         // swapped layout: rows per column
+    bool ok = false;
     if (warp < 4) {
         // Warp-uniform: tcgen05.ld below is .sync.aligned.
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull, 0, wc));
+        ok = __all_sync(0xffffffffu, mbar_wait(tfull, 0, wc));
         tc_fence_after_sync();
+    }
+    // Receive buffers inside the stage ring: every CTA's MMAs must be done
+    // (its tfull observed above) before anyone writes into it.
+    if (split_k && !Cfg::kRecvOwn) cluster_sync();
+    if (warp < 4) {
         if (ok) {
             const int r = warp * 32 + lane;   // accumulator row = TMEM lane
             const uint32_t t_row = tmem_base + ((warp * 32u) << 16);
-            float* red = reinterpret_cast<float*>(smem);
+            const int owner = ((r >> 2) * split + split - 1) >> 5;
+            const int lr = r - 4 * (owner * 32 / split);
+            const uint32_t recv = map_to_rank(smem_addr(smem + Cfg::kRecvOff), owner);
 #pragma unroll 1
             for (int c = 0; c < kBNm; c += Cfg::kChunk) {
                 uint32_t v[Cfg::kChunk];
@@ -443,13 +467,15 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
                     if constexpr (kSwap) {
 #pragma unroll
                         for (int j = 0; j < Cfg::kChunk; ++j)
-                            red[(c + j) * Cfg::kRedStride + r] = __uint_as_float(v[j]);
+                            st_dsmem_f32(recv + ((rank * kBNm + c + j) * sw_stride + lr) * 4u,
+                                         __uint_as_float(v[j]));
                     } else {
+                        const uint32_t row_off = (rank * nrows_max + lr) * (kBNm + 4);
 #pragma unroll
                         for (int j = 0; j < Cfg::kChunk; j += 4)
-                            *reinterpret_cast<float4*>(red + r * Cfg::kRedStride + c + j) =
-                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                            __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                            st_dsmem_f4(recv + (row_off + c + j) * 4u, __uint_as_float(v[j]),
+                                        __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                        __uint_as_float(v[j + 3]));
                     }
                 } else if constexpr (kSwap) {
                     store_col_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
@@ -462,51 +488,34 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     }
 
     if (split_k) {
-        // Every CTA of the cluster has its FP32 partial in shared memory; each
-        // reduces an equal slice of the tile over ranks 0..split-1 in order.
         cluster_sync();
-        const uint32_t rank = cluster_ctarank();
-        constexpr uint32_t kQuadsPerRow = kSwap ? (kMmaM / 4) : (kBNm / 4);
-        constexpr uint32_t kQuads = Cfg::kRedRows * kQuadsPerRow;
-        const uint32_t q0 = rank * kQuads / split, q1 = (rank + 1) * kQuads / split;
-        const uint32_t red_base = smem_addr(smem);
-        // kUnroll quads per thread and round keep that many remote loads in
-        // flight per rank (the loop is otherwise bound by DSMEM latency).
-        constexpr uint32_t kUnroll = 8;
-        for (uint32_t q = q0 + threadIdx.x; q < q1; q += kThreads * kUnroll) {
-            float4 acc[kUnroll];
-            uint32_t off[kUnroll];
-#pragma unroll
-            for (uint32_t u = 0; u < kUnroll; ++u) {
-                acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                const uint32_t qq = q + u * kThreads;
-                const uint32_t rr = qq / kQuadsPerRow, cc = (qq % kQuadsPerRow) * 4;
-                off[u] = red_base + (rr * Cfg::kRedStride + cc) * 4u;
-            }
-            for (int s = 0; s < split; ++s) {
-                float4 v[kUnroll];
-#pragma unroll
-                for (uint32_t u = 0; u < kUnroll; ++u)
-                    if (q + u * kThreads < q1) v[u] = ld_dsmem_f4(map_to_rank(off[u], s));
-#pragma unroll
-                for (uint32_t u = 0; u < kUnroll; ++u)
-                    if (q + u * kThreads < q1) {
-                        acc[u].x += v[u].x; acc[u].y += v[u].y; acc[u].z += v[u].z; acc[u].w += v[u].w;
-                    }
-            }
-#pragma unroll
-            for (uint32_t u = 0; u < kUnroll; ++u) {
-                const uint32_t qq = q + u * kThreads;
-                if (qq >= q1) break;
-                const uint32_t rr = qq / kQuadsPerRow, cc = (qq % kQuadsPerRow) * 4;
-                if constexpr (kSwap) {
-                    store_quad(p, acc_col0 + rr, acc_row0 + cc, acc[u]);   // row = m, cols = n
-                } else {
-                    store_quad(p, acc_row0 + rr, acc_col0 + cc, acc[u]);
+        const int first = 4 * (static_cast<int>(rank) * 32 / split);          // multiple of 4
+        const int nrows = 4 * ((static_cast<int>(rank) + 1) * 32 / split) - first;
+        const float* recv = reinterpret_cast<const float*>(smem + Cfg::kRecvOff);
+        if constexpr (kSwap) {
+            // Items: (output row m = accumulator column, 4 consecutive n).
+            const int quads = (nrows + 3) / 4;
+            for (int it = threadIdx.x; it < kBNm * quads; it += kThreads) {
+                const int m = it / quads, lq = (it - m * quads) * 4;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < split; ++s) {
+                    const float4 x = *reinterpret_cast<const float4*>(recv + (s * kBNm + m) * sw_stride + lq);
+                    acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
                 }
+                store_quad(p, acc_col0 + m, acc_row0 + first + lq, acc);   // lq + 4 <= nrows
+            }
+        } else {
+            constexpr int kQ = kBNm / 4;
+            for (int it = threadIdx.x; it < nrows * kQ; it += kThreads) {
+                const int lr = it / kQ, cq = (it - lr * kQ) * 4;
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s = 0; s < split; ++s) {
+                    const float4 x = *reinterpret_cast<const float4*>(recv + (s * nrows_max + lr) * (kBNm + 4) + cq);
+                    acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+                }
+                store_quad(p, acc_row0 + first + lr, acc_col0 + cq, acc);
             }
         }
-        cluster_sync();
     }
 
     __syncthreads();

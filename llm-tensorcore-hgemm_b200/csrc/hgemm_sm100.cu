@@ -204,8 +204,8 @@ KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
 // Swap-AB tiles for M <= 128 use at most ~110 KB of shared memory so that two
 // CTAs (of different clusters) share an SM; their TMEM (<= 128 columns
 // each) then fits twice into the 512 columns.
-KernelEntry g_swap_16 = HG_TILE(16, true, true, 6);
-KernelEntry g_swap_32 = HG_TILE(32, true, true, 5);
+KernelEntry g_swap_16 = HG_TILE(16, true, true, 5);
+KernelEntry g_swap_32 = HG_TILE(32, true, true, 4);
 KernelEntry g_swap_64 = HG_TILE(64, true, true, 4);
 KernelEntry g_swap_128 = HG_TILE(128, true, true, 3);
 KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
@@ -233,6 +233,53 @@ int choose_split(int64_t base_ctas, int64_t nkb, int sms, int max_split) {
     if (s > max_split) s = max_split;
     if (s > nkb) s = nkb;
     return static_cast<int>(s);
+}
+
+// How many clusters of `cluster` CTAs of kernel `k` fit on device `dev` at
+// once (cached). Clusters must fit inside one GPC, so large clusters of
+// SM-filling CTAs can fit fewer times than SMs / cluster suggests.
+int max_active_clusters(KernelEntry& k, int dev, int cluster) {
+    static std::mutex mu;
+    static std::unordered_map<uint64_t, int> cache;
+    const uint64_t key = (reinterpret_cast<uint64_t>(k.fn) << 12) ^ (static_cast<uint64_t>(dev) << 6) ^
+                         static_cast<uint64_t>(cluster);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    int n = 0;
+    if (prepare_kernel(k, dev) == HGEMM_SM100_OK) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(1, 1, static_cast<unsigned>(cluster));
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = k.smem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = static_cast<unsigned>(cluster);
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+        }
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = n;
+    return n;
+}
+
+// Lowers `split` until all `base` clusters of the tile kernel are resident at
+// once (a second wave of clusters would double the time), when possible.
+int fit_split(KernelEntry& k, int dev, int64_t base, int split) {
+    while (split > 1) {
+        const int n = max_active_clusters(k, dev, split);
+        if (n <= 0 || base <= n) break;
+        --split;
+    }
+    return split;
 }
 
 int check_args(const HgemmSm100Args* a) {
@@ -410,6 +457,14 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
         split = a.split_k > 0 ? a.split_k : choose_split(base, nkb, sms * per_sm, dev.max_cluster);
         if (split > nkb) split = static_cast<int32_t>(nkb);
         if (split < 1) split = 1;
+        if (a.split_k <= 0 && split > 1) {
+            KernelEntry* k = cfg == HGEMM_SM100_CFG_SWAPAB          ? swap_choice(a.m).k
+                             : cfg == HGEMM_SM100_CFG_SPLITK_128x256 ? &g_splitk_256
+                             : cfg == HGEMM_SM100_CFG_SPLITK_128x128 ? &g_splitk_128
+                                                                     : &g_generic_128;
+            int devid = 0;
+            if (cudaGetDevice(&devid) == cudaSuccess) split = fit_split(*k, devid, base, split);
+        }
     }
     *cfg_out = cfg;
     *split_out = split;

@@ -413,6 +413,17 @@ __device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
     return r;
 }
 
+// Stores to the shared memory of another CTA of the cluster (shared::cluster
+// address from map_to_rank); they complete asynchronously and become visible
+// to that CTA after a cluster barrier.
+__device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float a) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
+}
+
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"

@@ -1,0 +1,140 @@
+"""Model-level check: a random-init Qwen3-4B-architecture decoder with every
+``nn.Linear`` swapped for ``FrozenHgemmLinear``, against the stock model.
+
+Counterpart of the reference's model qualification
+(benchmarks/bench_integration.py:18-119: prefill and cached decode rollouts,
+``logits_gate`` with max-abs 0.05 and relative L2 0.001). No checkpoint is
+available here, so the weights are the architecture's own random init
+(normal, std 0.02) from a fixed seed; token ids are seeded random integers.
+
+    python llm-tensorcore-hgemm_b200/model_check.py            # Qwen3-4B sizes
+    python llm-tensorcore-hgemm_b200/model_check.py --layers 2 --hidden 256 ...
+
+Prints one JSON line: for prefill (batch 1 x 2048 tokens, last-token logits)
+and cached decode (batch 16, one token at context 2048), the logits gate of
+the swapped model against the stock model and both models' device times. The
+gate result is reported whether it passes or not.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
+
+import torch  # noqa: E402
+
+MAX_LOGIT_ABS = 0.05        # reference benchmarks/bench_integration.py:132
+MAX_LOGIT_REL_L2 = 0.001    # reference benchmarks/bench_integration.py:133
+
+
+def logits_gate(actual: list[torch.Tensor], expected: list[torch.Tensor],
+                max_abs: float = MAX_LOGIT_ABS, max_rel_l2: float = MAX_LOGIT_REL_L2) -> dict:
+    """Largest max-abs and relative-L2 logit error over the given steps; fails
+    on any non-finite logit (reference bench_integration.py:47-70)."""
+    worst_abs, worst_rel, finite = 0.0, 0.0, True
+    for a, e in zip(actual, expected):
+        a32, e32 = a.float(), e.float()
+        finite = finite and bool(torch.isfinite(a32).all())
+        d = a32 - e32
+        worst_abs = max(worst_abs, float(d.abs().max()))
+        worst_rel = max(worst_rel, float(torch.linalg.vector_norm(d) /
+                                         torch.linalg.vector_norm(e32).clamp_min(1e-12)))
+    ok = finite and worst_abs <= max_abs and worst_rel <= max_rel_l2
+    return {"correctness": "pass" if ok else "fail", "logits_finite": finite,
+            "logits_max_abs_error": worst_abs, "logits_max_relative_l2_error": worst_rel,
+            "max_abs_limit": max_abs, "max_relative_l2_limit": max_rel_l2}
+
+
+def build_model(args):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    cfg = Qwen3Config(
+        vocab_size=args.vocab, hidden_size=args.hidden, intermediate_size=args.intermediate,
+        num_hidden_layers=args.layers, num_attention_heads=args.heads,
+        num_key_value_heads=args.kv_heads, head_dim=args.head_dim, rms_norm_eps=1e-6,
+        rope_theta=1_000_000.0, max_position_embeddings=max(40960, args.context + 16),
+        tie_word_embeddings=True, attention_bias=False, initializer_range=0.02)
+    torch.manual_seed(args.seed)
+    with torch.device("cuda"):
+        model = Qwen3ForCausalLM(cfg).to(torch.float16).eval()
+    return model
+
+
+def timed(fn):
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    out = fn()
+    e.record()
+    e.synchronize()
+    return out, s.elapsed_time(e)
+
+
+@torch.inference_mode()
+def rollout(model, prompt, decode_prompts, decode_next):
+    """Last-token logits of a prefill, and decode-step logits for a batch of
+    sequences after a cached prefill of `decode_prompts`."""
+    pre, t_pre = timed(lambda: model(prompt, logits_to_keep=1).logits[:, -1].clone())
+    cache = model(decode_prompts, use_cache=True, logits_to_keep=1).past_key_values
+    torch.cuda.synchronize()
+    dec, t_dec = timed(lambda: model(decode_next, past_key_values=cache, use_cache=True,
+                                     logits_to_keep=1).logits[:, -1].clone())
+    del cache
+    return pre, dec, t_pre, t_dec
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--layers", type=int, default=36)
+    p.add_argument("--hidden", type=int, default=2560)
+    p.add_argument("--intermediate", type=int, default=9728)
+    p.add_argument("--heads", type=int, default=32)
+    p.add_argument("--kv-heads", type=int, default=8)
+    p.add_argument("--head-dim", type=int, default=128)
+    p.add_argument("--vocab", type=int, default=151936)
+    p.add_argument("--prefill-tokens", type=int, default=2048)
+    p.add_argument("--decode-batch", type=int, default=16)
+    p.add_argument("--context", type=int, default=2048)
+    p.add_argument("--seed", type=int, default=2026)
+    p.add_argument("--implementation", default="auto")
+    args = p.parse_args()
+
+    from llm_hgemm.integration import FrozenHgemmLinear, swap_linears
+
+    model = build_model(args)
+    g = torch.Generator(device="cuda").manual_seed(args.seed + 1)
+    prompt = torch.randint(0, args.vocab, (1, args.prefill_tokens), device="cuda", generator=g)
+    decode_prompts = torch.randint(0, args.vocab, (args.decode_batch, args.context), device="cuda",
+                                   generator=g)
+    decode_next = torch.randint(0, args.vocab, (args.decode_batch, 1), device="cuda", generator=g)
+
+    rollout(model, prompt, decode_prompts, decode_next)   # warm-up at full size
+    ref_pre, ref_dec, t_pre_ref, t_dec_ref = rollout(model, prompt, decode_prompts, decode_next)
+
+    swapped = swap_linears(model, args.implementation)
+    adapters = [m for m in model.modules() if isinstance(m, FrozenHgemmLinear)]
+    rollout(model, prompt, decode_prompts, decode_next)   # warm-up at full size
+    out_pre, out_dec, t_pre, t_dec = rollout(model, prompt, decode_prompts, decode_next)
+    backends = sorted({str(m.last_backend) for m in adapters})
+
+    result = {
+        "model": "Qwen3-4B architecture, random init (std 0.02), FP16",
+        "layers": args.layers, "hidden": args.hidden, "vocab": args.vocab,
+        "linears_swapped": swapped, "executed_backends": backends,
+        "implementation": args.implementation,
+        "prefill": {"tokens": args.prefill_tokens, **logits_gate([out_pre], [ref_pre]),
+                    "stock_ms": round(t_pre_ref, 3), "hgemm_ms": round(t_pre, 3)},
+        "decode": {"batch": args.decode_batch, "context": args.context,
+                   **logits_gate([out_dec], [ref_dec]),
+                   "stock_ms": round(t_dec_ref, 3), "hgemm_ms": round(t_dec, 3)},
+    }
+    print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

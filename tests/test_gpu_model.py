@@ -1,0 +1,55 @@
+"""Model-level use of the adapter: a small random-init Qwen3 decoder with
+every nn.Linear swapped for FrozenHgemmLinear (reference
+benchmarks/bench_integration.py:92-119 qualifies one module at a time; here
+all of them), prefill and cached decode against the stock model."""
+
+import argparse
+import importlib.util
+
+import pytest
+import torch
+
+from tests.conftest import PKG
+from tests.gpu_helpers import require_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+def load_model_check():
+    spec = importlib.util.spec_from_file_location("model_check", PKG / "model_check.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_small_qwen3_swapped_matches_stock():
+    require_cuda()
+    mc = load_model_check()
+    from llm_hgemm.integration import FrozenHgemmLinear, swap_linears
+
+    args = argparse.Namespace(vocab=1000, hidden=256, intermediate=704, layers=2, heads=4,
+                              kv_heads=2, head_dim=64, context=64, seed=3)
+    model = mc.build_model(args)
+    g = torch.Generator(device="cuda").manual_seed(4)
+    prompt = torch.randint(0, 1000, (1, 96), device="cuda", generator=g)
+    dprompts = torch.randint(0, 1000, (4, 64), device="cuda", generator=g)
+    dnext = torch.randint(0, 1000, (4, 1), device="cuda", generator=g)
+    ref_pre, ref_dec, _, _ = mc.rollout(model, prompt, dprompts, dnext)
+    n = swap_linears(model, "auto")
+    assert n == 2 * 7 + 1              # q, k, v, o, gate, up, down per layer + lm_head
+    out_pre, out_dec, _, _ = mc.rollout(model, prompt, dprompts, dnext)
+    adapters = [m for m in model.modules() if isinstance(m, FrozenHgemmLinear)]
+    assert all(m.last_backend == "auto" for m in adapters)
+    for out, ref in ((out_pre, ref_pre), (out_dec, ref_dec)):
+        gate = mc.logits_gate([out], [ref], max_abs=0.05, max_rel_l2=0.01)
+        assert gate["correctness"] == "pass", gate
+
+
+def test_logits_gate_rejects_nonfinite_and_large_errors():
+    mc = load_model_check()
+    ref = torch.ones(4, 8)
+    assert mc.logits_gate([ref.clone()], [ref])["correctness"] == "pass"
+    bad = ref.clone()
+    bad[0, 0] = float("nan")
+    assert mc.logits_gate([bad], [ref])["logits_finite"] is False
+    assert mc.logits_gate([ref * 1.004], [ref])["correctness"] == "fail"
