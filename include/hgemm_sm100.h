@@ -64,7 +64,9 @@ enum {
                                               stream-K ranges (workspace)       */
     HGEMM_SM100_CFG_STREAMK_SWAPAB = 9,    /* "tc_streamk_swapab": the same with
                                               C^T = B^T A^T, M <= 128           */
-    HGEMM_SM100_CFG_COUNT = 10
+    HGEMM_SM100_CFG_PAIR_256x128 = 10,     /* "tc_pair_256x128": CTA pair, 256 x 128
+                                              tiles (one wave for mid-size M)   */
+    HGEMM_SM100_CFG_COUNT = 11
 };
 
 /* Flags. */

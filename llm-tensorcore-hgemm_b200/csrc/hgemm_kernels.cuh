@@ -704,37 +704,40 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
 
 // ============================================== CTA-pair persistent kernel ====
 //
-// 256 x 256 output tiles per cluster of two CTAs (cta_group::2). CTA r of the
-// pair TMA-loads rows 128r .. 128r+127 of the A tile and columns 128r ..
-// 128r+127 of the B tile into its own shared memory; the even CTA's single
-// MMA thread issues M=256, N=256 MMAs that read both CTAs' tiles, and each
-// CTA's TMEM receives its own 128 accumulator rows (two 256-column buffers).
+// 256 x kTileN output tiles (kTileN = 256 or 128) per cluster of two CTAs
+// (cta_group::2). CTA r of the pair TMA-loads rows 128r .. 128r+127 of the A
+// tile and the r-th kTileN/2 columns of the B tile into its own shared
+// memory; the even CTA's single MMA thread issues M=256, N=kTileN MMAs that
+// read both CTAs' tiles, and each CTA's TMEM receives its own 128 accumulator
+// rows (two kTileN-column buffers).
 // Both CTAs' loads complete their bytes on the even CTA's "stage full"
 // barrier (armed once with both CTAs' bytes); the MMA thread commits "stage
 // empty" and "accumulator full" to the barriers of both CTAs; one lane per
 // epilogue warp of either CTA arrives on the even CTA's "accumulator empty".
 
-template <int kStages>
+template <int kTileNT, int kStages>
 struct PairCfg {
-    static constexpr int kTileM = 256, kTileN = 256;
+    static constexpr int kTileM = 256, kTileN = kTileNT;   // pair tile; each CTA: 128 x kTileN
+    static constexpr int kHalfN = kTileN / 2;              // B columns each CTA loads
     static constexpr uint32_t kABytes = 128u * 128u;        // 128 rows x 64 halves
-    static constexpr uint32_t kBBytes = 128u * 128u;        // 64 k-rows x 128 halves
+    static constexpr uint32_t kBBytes = kHalfN * 128u;      // 64 k-rows x kHalfN halves
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kEpiBytes = 4u * 2u * 4096u;   // 4 warps x 2 boxes of 32 x 64 halves
     static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
-    static constexpr uint32_t kTmemCols = 512;              // 2 x 256 FP32 columns
-    static constexpr uint32_t kIdesc = make_idesc_f16(256, 256, false, true);
+    static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kTileN);   // 2 accumulators
+    static constexpr uint32_t kIdesc = make_idesc_f16(256, kTileN, false, true);
+    static_assert(kTileN == 128 || kTileN == 256, "pair tile width");
     static_assert(2 * kStages + 5 <= 30, "barrier area");
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
-template <int kStages>
+template <int kTileNT, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-    using Cfg = PairCfg<kStages>;
+    using Cfg = PairCfg<kTileNT, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);   // even CTA
@@ -790,7 +793,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 int tm, tn;
                 tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
                 const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * 128;
-                const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * 128;
+                const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
                     uint8_t* s_a = smem + stage * Cfg::kStageBytes;
@@ -801,8 +804,9 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                         mbar_arrive_expect_tx(&full[stage], 2u * Cfg::kStageBytes + extra);
                     }
                     tma_load_2d_pair(s_a, &tm_a, bar, kb * kBlockK, row0);
-                    tma_load_2d_pair(s_b, &tm_b, bar, col0, kb * kBlockK);
-                    tma_load_2d_pair(s_b + kChunkBytes, &tm_b, bar, col0 + 64, kb * kBlockK);
+#pragma unroll
+                    for (int j = 0; j < Cfg::kHalfN / 64; ++j)
+                        tma_load_2d_pair(s_b + j * kChunkBytes, &tm_b, bar, col0 + 64 * j, kb * kBlockK);
                     ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1u; }
                 }

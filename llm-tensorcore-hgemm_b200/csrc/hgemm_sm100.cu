@@ -39,6 +39,7 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_splitk_128x256",
     "tc_streamk_128x256",
     "tc_streamk_swapab",
+    "tc_pair_256x128",
 };
 
 // ------------------------------------------------------ device properties --
@@ -175,9 +176,9 @@ int prepare_kernel(KernelEntry& k, int dev) {
         reinterpret_cast<const void*>(&hgemm_tile_kernel<BN, SWAP, TMA, ST>),              \
             TileCfg<BN, SWAP, TMA, ST>::kSmemBytes                                         \
     }
-#define HG_PAIR(ST)                                                                       \
+#define HG_PAIR(BN, ST)                                                                   \
     KernelEntry {                                                                          \
-        reinterpret_cast<const void*>(&hgemm_pair_kernel<ST>), PairCfg<ST>::kSmemBytes     \
+        reinterpret_cast<const void*>(&hgemm_pair_kernel<BN, ST>), PairCfg<BN, ST>::kSmemBytes \
     }
 #define HG_STREAMK(BN, SWAP, ST)                                                          \
     KernelEntry {                                                                          \
@@ -190,7 +191,8 @@ int prepare_kernel(KernelEntry& k, int dev) {
             PersistCfg<BN, ST>::kSmemBytes                                                 \
     }
 
-KernelEntry g_pair_256 = HG_PAIR(6);
+KernelEntry g_pair_256 = HG_PAIR(256, 6);
+KernelEntry g_pair_128 = HG_PAIR(128, 8);
 KernelEntry g_sk_256 = HG_STREAMK(256, false, 4);
 KernelEntry g_sk_swap_16 = HG_STREAMK(16, true, 10);
 KernelEntry g_sk_swap_32 = HG_STREAMK(32, true, 9);
@@ -574,17 +576,19 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             const int64_t grid = tiles < dev.sms ? tiles : dev.sms;
             return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, map_c, p, stream);
         }
-        case HGEMM_SM100_CFG_PAIR_256x256: {
+        case HGEMM_SM100_CFG_PAIR_256x256:
+        case HGEMM_SM100_CFG_PAIR_256x128: {
+            const bool wide = cfg == HGEMM_SM100_CFG_PAIR_256x256;
+            KernelEntry& k = wide ? g_pair_256 : g_pair_128;
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
-            if ((rc = prepare_kernel(g_pair_256, devid)) != HGEMM_SM100_OK) return rc;
-            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, 256);
+            if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
+            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, wide ? 256 : 128);
             const int64_t pairs_max = dev.sms / 2;
             const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
             p.group_m = 8;
-            return launch(g_pair_256, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, map_c, p,
-                          stream, 2);
+            return launch(k, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, map_c, p, stream, 2);
         }
         case HGEMM_SM100_CFG_SPLITK_128x128:
         case HGEMM_SM100_CFG_SPLITK_128x256: {

@@ -33,6 +33,7 @@ CFG_PAIR_256x256 = 6
 CFG_SPLITK_128x256 = 7
 CFG_STREAMK_128x256 = 8
 CFG_STREAMK_SWAPAB = 9
+CFG_PAIR_256x128 = 10
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2

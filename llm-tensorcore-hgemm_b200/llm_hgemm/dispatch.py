@@ -38,6 +38,7 @@ CUSTOM_PROVIDERS = (
     "tc_splitk_128x256",
     "tc_streamk_128x256",
     "tc_streamk_swapab",
+    "tc_pair_256x128",
 )
 MISALIGNED_PROVIDER = "auto"
 DEFAULT_PROVIDER = "auto"

@@ -17,6 +17,7 @@ IMPLEMENTATIONS = [
     "tc_splitk_128x256",
     "tc_streamk_128x256",
     "tc_streamk_swapab",
+    "tc_pair_256x128",
 ]
 
 

@@ -25,6 +25,7 @@ CONFIG_IDS = {
     "tc_splitk_128x256": capi.CFG_SPLITK_128x256,
     "tc_streamk_128x256": capi.CFG_STREAMK_128x256,
     "tc_streamk_swapab": capi.CFG_STREAMK_SWAPAB,
+    "tc_pair_256x128": capi.CFG_PAIR_256x128,
 }
 
 
