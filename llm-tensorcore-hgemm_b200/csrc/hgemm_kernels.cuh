@@ -185,6 +185,27 @@ __device__ __forceinline__ void store_box_tma(const CUtensorMap* map, uint8_t* b
     }
 }
 
+// Swapped-tile epilogue box: kRows output rows (accumulator columns) x 32
+// output columns (the warp's 32 accumulator rows); lane l holds column
+// n0 + l, v[j] for row m0 + j. Staged densely ([row][32] halves, 64-byte
+// rows, unswizzled map) and written by one TMA store (which clips at the
+// matrix edges). Double-buffered per warp like store_box_tma.
+template <int kRows>
+__device__ __forceinline__ void store_box_tma_t(const CUtensorMap* map, uint8_t* box, uint32_t lane,
+                                                const uint32_t* v, int n0, int m0) {
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    __half* h = reinterpret_cast<__half*>(box);
+#pragma unroll
+    for (int j = 0; j < kRows; ++j) h[j * 32 + lane] = __float2half_rn(__uint_as_float(v[j]));
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(map, box, n0, m0);
+        bulk_commit_group();
+    }
+}
+
 // ------------------------------------------------- generic tile loaders ----
 
 // K-major tile: rows r0 .. r0 + kRows - 1 of the row-major [rows x K] matrix x,
@@ -297,6 +318,10 @@ struct TileCfg {
     static constexpr bool kRecvOwn = kSwap && kBNm <= 32;
     static constexpr uint32_t kRecvBytes = kSwap ? 180u * kBNm * 4u : 180u * (kBNm + 4) * 4u;
     static constexpr uint32_t kRecvOff = kRecvOwn ? kStages * kStageBytes : 0u;
+    // Workspace exchange: one FP32 tile per CTA, staged in the stage ring.
+    static constexpr uint32_t kSlotFloats = kSwap ? 128u * kBNm : 128u * (kBNm + 4);
+    static_assert(kSlotFloats * 4u <= kStages * kStageBytes, "staging fits the stage ring");
+    static_assert(kSwap || kStages * kStageBytes >= 4u * 8192u, "TMA-store boxes fit the stage ring");
     static constexpr uint32_t kDataBytes =
         kRecvOwn ? kStages * kStageBytes + kRecvBytes : cmax(kStages * kStageBytes, kRecvBytes);
     static constexpr uint32_t kBarBytes = 256;
@@ -311,13 +336,77 @@ struct TileCfg {
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
+// Split-K reduction of the rows this CTA owns (first .. first + nrows - 1 of
+// the accumulator tile) from the receive buffer, summed over ranks
+// 0..split-1 in order, stored to C. Receive layouts: [rank][local row][kBNm
+// + 4] floats, rank stride nrows_max rows; swapped [rank][col][local row],
+// rank stride kBNm * nrows_max, column stride sw_stride. All threads of the
+// CTA take part.
+template <int kBNm, bool kSwap>
+__device__ __forceinline__ void reduce_owned_rows(const GemmParams& p, const float* recv, int split, int nrows,
+                                                  int nrows_max, int sw_stride, int first, int acc_row0,
+                                                  int acc_col0) {
+    // kU independent items per thread per step (loads of all of them are in
+    // flight together); out-of-range item slots load item 0 and store nothing.
+    constexpr int kU = 4;
+    const int rank_stride = kSwap ? kBNm * nrows_max : nrows_max * (kBNm + 4);
+    // Fast store path: FP16, 16-byte-aligned rows, tile inside C.
+    const int rows_total = kSwap ? p.n : p.m;
+    const int cols_total = kSwap ? p.m : p.n;
+    const bool fast = !p.out_f32 && p.vec_ok && acc_row0 + first + nrows <= rows_total && acc_col0 + kBNm <= cols_total;
+    const int quads = nrows >> 2;                         // nrows is a multiple of 4
+    const int total = kSwap ? kBNm * quads : nrows * (kBNm / 4);
+    for (int base = threadIdx.x; base < total; base += kU * kThreads) {
+        float4 acc[kU];
+        int off[kU], row[kU], col[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const int it = base + u * kThreads < total ? base + u * kThreads : 0;
+            if constexpr (kSwap) {
+                // (output row m = accumulator column, 4 consecutive n)
+                const int m = it / quads, lq = (it - m * quads) * 4;
+                off[u] = m * sw_stride + lq;
+                row[u] = acc_col0 + m;
+                col[u] = acc_row0 + first + lq;
+            } else {
+                constexpr int kQ = kBNm / 4;
+                const int lr = it / kQ, cq = (it - lr * kQ) * 4;
+                off[u] = lr * (kBNm + 4) + cq;
+                row[u] = acc_row0 + first + lr;
+                col[u] = acc_col0 + cq;
+            }
+            acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        for (int s = 0; s < split; ++s) {
+            const float* rs = recv + s * rank_stride;
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const float4 x = *reinterpret_cast<const float4*>(rs + off[u]);
+                acc[u].x += x.x; acc[u].y += x.y; acc[u].z += x.z; acc[u].w += x.w;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (base + u * kThreads >= total) break;
+            if (fast) {
+                uint2 q;
+                q.x = pack_half2(__float_as_uint(acc[u].x), __float_as_uint(acc[u].y));
+                q.y = pack_half2(__float_as_uint(acc[u].z), __float_as_uint(acc[u].w));
+                *reinterpret_cast<uint2*>(static_cast<__half*>(p.c) + static_cast<long long>(row[u]) * p.ldc +
+                                          col[u]) = q;
+            } else {
+                store_quad(p, row[u], col[u], acc[u]);
+            }
+        }
+    }
+}
+
 // Grid: x = 128-row accumulator tiles (M tiles, or N tiles when swapped),
 // y = kBNm-wide accumulator column tiles, z = K splits (== cluster size).
 template <int kBNm, bool kSwap, bool kTma, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_mn,
                   const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-    (void)tm_c;
     using Cfg = TileCfg<kBNm, kSwap, kTma, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
@@ -429,93 +518,185 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     __syncwarp();
 
     // --------------------------------------------------------- epilogue --
-    // Without a split the accumulator goes straight to C. With a K split,
-    // every CTA pushes each accumulator row into the receive buffer of the CTA
-    // that owns the row (remote shared-memory stores, no waiting), one cluster
-    // barrier makes them visible, and each CTA sums its rows over ranks
-    // 0..split-1 in order (deterministic) and stores them.
+    // Without a split the accumulator goes to C: through per-warp shared-memory
+    // boxes and TMA stores when C allows it (p.tma_store), else with direct
+    // stores. With a K split the accumulator rows are divided among the CTAs
+    // of the cluster in whole quads (rank r owns rows from 4 * (r * 32 / split));
+    // each CTA sums its rows over ranks 0..split-1 in rank order
+    // (deterministic) and stores them. The partial tiles travel
+    //  * through the caller's workspace when there is one (p.partials): each
+    //    CTA stages its FP32 tile in shared memory, grouped by owning rank,
+    //    copies it to its workspace slot with one bulk copy and, after a
+    //    cluster barrier, bulk-loads the rows it owns from every rank's slot;
+    //  * else through distributed shared memory: every CTA pushes each row
+    //    into the receive buffer of its owner with remote stores, and one
+    //    cluster barrier makes them visible.
+    // The stage ring is idle once tfull has completed (every MMA has read its
+    // operands), so boxes, staging and receive buffers reuse it.
     const bool split_k = split > 1;
+    const bool via_l2 = split_k && p.partials != nullptr;
     const uint32_t rank = cluster_ctarank();
     const int nrows_max = 4 * ((32 + split - 1) / split);   // rows owned per rank, bound
-    const int sw_stride = nrows_max;                         // swapped layout: rows per column
+    const int first = 4 * (static_cast<int>(rank) * 32 / split);          // multiple of 4
+    const int nrows = 4 * ((static_cast<int>(rank) + 1) * 32 / split) - first;
+    // Swapped receive layout [rank][col][local row]: column stride.
+    const int sw_stride = via_l2 ? nrows : nrows_max;
+    volatile int* xchg_go = abort_flag + 1;   // workspace exchange proceeds
     bool ok = false;
     if (warp < 4) {
         // Warp-uniform: tcgen05.ld below is .sync.aligned.
         ok = __all_sync(0xffffffffu, mbar_wait(tfull, 0, wc));
         tc_fence_after_sync();
     }
-    // Receive buffers inside the stage ring: every CTA's MMAs must be done
-    // (its tfull observed above) before anyone writes into it.
-    if (split_k && !Cfg::kRecvOwn) cluster_sync();
+    // Push receive buffers inside the stage ring: every CTA's MMAs must be
+    // done (its tfull observed above) before anyone writes into it.
+    if (split_k && !via_l2 && !Cfg::kRecvOwn) cluster_sync();
     if (warp < 4) {
         if (ok) {
             const int r = warp * 32 + lane;   // accumulator row = TMEM lane
             const uint32_t t_row = tmem_base + ((warp * 32u) << 16);
             const int owner = ((r >> 2) * split + split - 1) >> 5;
-            const int lr = r - 4 * (owner * 32 / split);
-            const uint32_t recv = map_to_rank(smem_addr(smem + Cfg::kRecvOff), owner);
+            const int o_first = 4 * (owner * 32 / split);
+            const int lr = r - o_first;
+            if (!split_k && p.tma_store) {
+                uint8_t* boxes = smem + warp * 8192u;
+                uint32_t buf = 0;
+                if constexpr (kSwap) {
 #pragma unroll 1
-            for (int c = 0; c < kBNm; c += Cfg::kChunk) {
-                uint32_t v[Cfg::kChunk];
-                if constexpr (Cfg::kChunk == 32) {
-                    tmem_ld_32x32b_x32(t_row + c, v);
-                } else {
-                    tmem_ld_32x32b_x16(t_row + c, v);
-                }
-                tmem_wait_ld();
-                if (split_k) {
-                    if constexpr (kSwap) {
-#pragma unroll
-                        for (int j = 0; j < Cfg::kChunk; ++j)
-                            st_dsmem_f32(recv + ((rank * kBNm + c + j) * sw_stride + lr) * 4u,
-                                         __uint_as_float(v[j]));
-                    } else {
-                        const uint32_t row_off = (rank * nrows_max + lr) * (kBNm + 4);
-#pragma unroll
-                        for (int j = 0; j < Cfg::kChunk; j += 4)
-                            st_dsmem_f4(recv + (row_off + c + j) * 4u, __uint_as_float(v[j]),
-                                        __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
-                                        __uint_as_float(v[j + 3]));
+                    for (int c = 0; c < kBNm; c += Cfg::kChunk) {
+                        uint32_t v[Cfg::kChunk];
+                        if constexpr (Cfg::kChunk == 32) tmem_ld_32x32b_x32(t_row + c, v);
+                        else tmem_ld_32x32b_x16(t_row + c, v);
+                        tmem_wait_ld();
+                        store_box_tma_t<Cfg::kChunk>(&tm_c, boxes + buf * 2048u, lane, v,
+                                                     acc_row0 + static_cast<int>(warp) * 32, acc_col0 + c);
+                        buf ^= 1u;
                     }
-                } else if constexpr (kSwap) {
-                    store_col_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
                 } else {
-                    store_row_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
+#pragma unroll 1
+                    for (int c = 0; c < kBNm; c += 64) {
+                        uint32_t v0[32], v1[32];
+                        tmem_ld_32x32b_x32(t_row + c, v0);
+                        tmem_ld_32x32b_x32(t_row + c + 32, v1);
+                        tmem_wait_ld();
+                        store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, acc_col0 + c,
+                                      acc_row0 + static_cast<int>(warp) * 32);
+                        buf ^= 1u;
+                    }
+                }
+                if (lane == 0) bulk_wait_group_all();
+            } else {
+                float* stage_f = reinterpret_cast<float*>(smem);
+                const uint32_t recv = map_to_rank(smem_addr(smem + Cfg::kRecvOff), owner);
+                const int o_rows = 4 * ((owner + 1) * 32 / split) - o_first;
+#pragma unroll 1
+                for (int c = 0; c < kBNm; c += Cfg::kChunk) {
+                    uint32_t v[Cfg::kChunk];
+                    if constexpr (Cfg::kChunk == 32) {
+                        tmem_ld_32x32b_x32(t_row + c, v);
+                    } else {
+                        tmem_ld_32x32b_x16(t_row + c, v);
+                    }
+                    tmem_wait_ld();
+                    if (via_l2) {
+                        if constexpr (kSwap) {
+                            // Owner blocks [col][local row], block o at kBNm * o_first.
+                            float* dst = stage_f + kBNm * o_first + lr;
+#pragma unroll
+                            for (int j = 0; j < Cfg::kChunk; ++j)
+                                dst[(c + j) * o_rows] = __uint_as_float(v[j]);
+                        } else {
+                            // Rows of kBNm + 4 floats (owner blocks are row ranges).
+                            float* dst = stage_f + r * (kBNm + 4) + c;
+#pragma unroll
+                            for (int j = 0; j < Cfg::kChunk; j += 4)
+                                *reinterpret_cast<uint4*>(dst + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    } else if (split_k) {
+                        if constexpr (kSwap) {
+#pragma unroll
+                            for (int j = 0; j < Cfg::kChunk; ++j)
+                                st_dsmem_f32(recv + ((rank * kBNm + c + j) * sw_stride + lr) * 4u,
+                                             __uint_as_float(v[j]));
+                        } else {
+                            const uint32_t row_off = (rank * nrows_max + lr) * (kBNm + 4);
+#pragma unroll
+                            for (int j = 0; j < Cfg::kChunk; j += 4)
+                                st_dsmem_f4(recv + (row_off + c + j) * 4u, __uint_as_float(v[j]),
+                                            __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                            __uint_as_float(v[j + 3]));
+                        }
+                    } else if constexpr (kSwap) {
+                        store_col_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
+                    } else {
+                        store_row_segment<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
+                    }
+                }
+                if (via_l2) {
+                    fence_async_shared();   // staging -> bulk copy (async proxy)
+                    if constexpr (!kSwap) {
+                        // This warp's 32 staged rows are contiguous: store them now.
+                        __syncwarp();
+                        if (lane == 0) {
+                            const size_t slot = blockIdx.x + static_cast<size_t>(gridDim.x) *
+                                                                 (blockIdx.y + static_cast<size_t>(gridDim.y) * rank);
+                            const uint32_t off = warp * 32u * (kBNm + 4);
+                            bulk_store(p.partials + slot * Cfg::kSlotFloats + off, stage_f + off,
+                                       32u * (kBNm + 4) * 4u);
+                            bulk_commit_group();
+                            bulk_wait_group_all();
+                            fence_async_global();
+                        }
+                    }
                 }
             }
         }
         tc_fence_before_sync();
     }
 
-    if (split_k) {
-        cluster_sync();
-        const int first = 4 * (static_cast<int>(rank) * 32 / split);          // multiple of 4
-        const int nrows = 4 * ((static_cast<int>(rank) + 1) * 32 / split) - first;
-        const float* recv = reinterpret_cast<const float*>(smem + Cfg::kRecvOff);
+    if (via_l2) {
+        // Slot of CTA (x, y, z): x + gridDim.x * (y + gridDim.y * z); the
+        // cluster spans z, so rank s of this cluster is z = s.
+        const size_t slot0 = blockIdx.x + static_cast<size_t>(gridDim.x) * blockIdx.y;
+        const size_t zstride = static_cast<size_t>(gridDim.x) * gridDim.y;
         if constexpr (kSwap) {
-            // Items: (output row m = accumulator column, 4 consecutive n).
-            const int quads = (nrows + 3) / 4;
-            for (int it = threadIdx.x; it < kBNm * quads; it += kThreads) {
-                const int m = it / quads, lq = (it - m * quads) * 4;
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int s = 0; s < split; ++s) {
-                    const float4 x = *reinterpret_cast<const float4*>(recv + (s * kBNm + m) * sw_stride + lq);
-                    acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-                }
-                store_quad(p, acc_col0 + m, acc_row0 + first + lq, acc);   // lq + 4 <= nrows
-            }
-        } else {
-            constexpr int kQ = kBNm / 4;
-            for (int it = threadIdx.x; it < nrows * kQ; it += kThreads) {
-                const int lr = it / kQ, cq = (it - lr * kQ) * 4;
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int s = 0; s < split; ++s) {
-                    const float4 x = *reinterpret_cast<const float4*>(recv + (s * nrows_max + lr) * (kBNm + 4) + cq);
-                    acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
-                }
-                store_quad(p, acc_row0 + first + lr, acc_col0 + cq, acc);
+            // Owner-grouped staging spans all warps' rows: one bulk copy.
+            if (warp < 4) epilogue_bar_sync();
+            if (threadIdx.x == 0 && *abort_flag == 0) {
+                bulk_store(p.partials + (slot0 + zstride * rank) * Cfg::kSlotFloats, smem,
+                           Cfg::kSlotFloats * 4u);
+                bulk_commit_group();
+                bulk_wait_group_all();
+                fence_async_global();
             }
         }
+        // A pipeline that gave up leaves its slot unwritten: skip the loads
+        // (the status word already records the failure).
+        if (threadIdx.x == 0) *xchg_go = *abort_flag == 0;
+        __syncwarp();
+        cluster_sync();   // every slot of the cluster written (release / acquire)
+        const bool go = *xchg_go != 0;
+        float* recv = reinterpret_cast<float*>(smem + Cfg::kRecvOff);
+        if (go && threadIdx.x == 0) {
+            fence_async_global();
+            const uint32_t row_floats = kSwap ? kBNm : kBNm + 4;   // floats per owned row
+            const uint32_t bytes = static_cast<uint32_t>(nrows) * row_floats * 4u;
+            mbar_arrive_expect_tx(tfull, bytes * static_cast<uint32_t>(split));
+            for (int s2 = 0; s2 < split; ++s2) {
+                const float* src = p.partials + (slot0 + zstride * s2) * Cfg::kSlotFloats +
+                                   static_cast<size_t>(first) * row_floats;
+                bulk_load(recv + static_cast<size_t>(s2) * nrows_max * row_floats, src, bytes, tfull);
+            }
+        }
+        // Every thread of the CTA reduces; the wait is bounded like any other.
+        ok = go && mbar_wait(tfull, 1, wc);
+        // After a timeout, the issuing thread lets its copies land (bounded).
+        if (go && !ok && threadIdx.x == 0) mbar_wait_drain(tfull, 1, kDrainLimitNs);
+        if (ok) reduce_owned_rows<kBNm, kSwap>(p, recv, split, nrows, nrows_max, sw_stride, first, acc_row0, acc_col0);
+    } else if (split_k) {
+        cluster_sync();
+        const float* recv = reinterpret_cast<const float*>(smem + Cfg::kRecvOff);
+        reduce_owned_rows<kBNm, kSwap>(p, recv, split, nrows, nrows_max, sw_stride, first, acc_row0, acc_col0);
     }
 
     __syncthreads();

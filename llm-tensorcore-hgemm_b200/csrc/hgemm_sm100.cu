@@ -99,9 +99,10 @@ struct MapKey {
     const void* base;
     uint64_t inner, outer, ld;
     uint32_t box_inner, box_outer;
+    bool swizzle;
     bool operator==(const MapKey& o) const {
         return base == o.base && inner == o.inner && outer == o.outer && ld == o.ld &&
-               box_inner == o.box_inner && box_outer == o.box_outer;
+               box_inner == o.box_inner && box_outer == o.box_outer && swizzle == o.swizzle;
     }
 };
 struct MapKeyHash {
@@ -111,18 +112,19 @@ struct MapKeyHash {
         h ^= (k.outer * 0xC2B2AE3D27D4EB4Full) + (h << 6) + (h >> 2);
         h ^= (k.ld * 0x165667B19E3779F9ull) + (h << 6) + (h >> 2);
         h ^= (static_cast<size_t>(k.box_inner) << 32 | k.box_outer) + (h << 6) + (h >> 2);
+        h ^= static_cast<size_t>(k.swizzle);
         return h;
     }
 };
 
 // 2-D FP16 row-major matrix [outer x inner] with row pitch `ld` elements,
-// 128-byte swizzled boxes of [box_outer x box_inner]; out-of-range elements
-// read as zero. Descriptors are cached per thread (they depend only on the
+// 128-byte swizzled (or, with swizzle false, dense row-major) boxes of
+// [box_outer x box_inner]; out-of-range elements read as zero. Descriptors are cached per thread (they depend only on the
 // key, so a reused address with the same shape reuses a valid descriptor).
 int tensor_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
-               uint32_t box_inner, uint32_t box_outer) {
+               uint32_t box_inner, uint32_t box_outer, bool swizzle = true) {
     thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-    const MapKey key{base, inner, outer, ld, box_inner, box_outer};
+    const MapKey key{base, inner, outer, ld, box_inner, box_outer, swizzle};
     auto it = cache.find(key);
     if (it != cache.end()) {
         *out = it->second;
@@ -137,7 +139,8 @@ int tensor_map(CUtensorMap* out, const void* base, uint64_t inner, uint64_t oute
     CUtensorMap map;
     const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims,
                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return HGEMM_SM100_ERR_TENSOR_MAP;
     if (cache.size() >= 256) cache.clear();
@@ -208,8 +211,8 @@ KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
 // each) then fits twice into the 512 columns.
 KernelEntry g_swap_16 = HG_TILE(16, true, true, 5);
 KernelEntry g_swap_32 = HG_TILE(32, true, true, 4);
-KernelEntry g_swap_64 = HG_TILE(64, true, true, 4);
-KernelEntry g_swap_128 = HG_TILE(128, true, true, 3);
+KernelEntry g_swap_64 = HG_TILE(64, true, true, 9);
+KernelEntry g_swap_128 = HG_TILE(128, true, true, 7);
 KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
 
 struct SwapChoice {
@@ -220,8 +223,8 @@ struct SwapChoice {
 SwapChoice swap_choice(int64_t m) {
     if (m <= 16) return {16, &g_swap_16, 2};
     if (m <= 32) return {32, &g_swap_32, 2};
-    if (m <= 64) return {64, &g_swap_64, 2};
-    if (m <= 128) return {128, &g_swap_128, 2};
+    if (m <= 64) return {64, &g_swap_64, 1};
+    if (m <= 128) return {128, &g_swap_128, 1};
     return {256, &g_swap_256, 1};
 }
 
@@ -340,6 +343,36 @@ StreamKPlan plan_streamk(int32_t cfg, int64_t m, int64_t n, int64_t k, int sms) 
     return sp;
 }
 
+// Split-K tile kernels: workspace for exchanging FP32 partial tiles, one slot
+// per CTA (0 when there is no split). Without it the partials go through
+// distributed shared memory.
+bool is_tile_cfg(int32_t cfg) {
+    return cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_SPLITK_128x256 ||
+           cfg == HGEMM_SM100_CFG_GENERIC_128x128 || cfg == HGEMM_SM100_CFG_SWAPAB;
+}
+
+size_t exchange_bytes(int32_t cfg, int64_t m, int64_t n, int32_t split) {
+    if (!is_tile_cfg(cfg) || split <= 1) return 0;
+    int64_t ctas;
+    size_t slot;
+    if (cfg == HGEMM_SM100_CFG_SWAPAB) {
+        const int bnm = swap_choice(m).bnm;
+        ctas = cdiv(n, 128) * cdiv(m, bnm);
+        slot = static_cast<size_t>(128) * bnm * 4;
+    } else {
+        const int bn = cfg == HGEMM_SM100_CFG_SPLITK_128x256 ? 256 : 128;
+        ctas = cdiv(m, 128) * cdiv(n, bn);
+        slot = static_cast<size_t>(128) * (bn + 4) * 4;
+    }
+    return static_cast<size_t>(ctas) * split * slot;
+}
+
+// Bytes of the kernel's own workspace region (after any staging buffers).
+size_t region_need(int32_t cfg, int32_t split, int64_t m, int64_t n, int64_t k, int sms) {
+    if (is_streamk(cfg)) return plan_streamk(cfg, m, n, k, sms).bytes;
+    return exchange_bytes(cfg, m, n, split);
+}
+
 std::atomic<uint64_t> g_epoch_counter{0};
 
 // A value no earlier launch of this process used (and, with the random base,
@@ -429,6 +462,14 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             cfg = tiles >= 4 * static_cast<int64_t>(sms) ? HGEMM_SM100_CFG_PERSISTENT_128x256
                   : tiles >= sms                         ? HGEMM_SM100_CFG_STREAMK_128x256
                                                          : HGEMM_SM100_CFG_SPLITK_128x256;
+            // Narrow tiles when they (with their K split) fill the SMs in one
+            // wave: the same MMA time per K block, half the partial tile to
+            // exchange, or no split at all.
+            if (cfg == HGEMM_SM100_CFG_SPLITK_128x256) {
+                const int64_t narrow = cdiv(a.m, 128) * cdiv(a.n, 128);
+                const int64_t ctas = narrow * choose_split(narrow, nkb, sms, dev.max_cluster);
+                if (narrow <= sms && 5 * ctas >= 4 * static_cast<int64_t>(sms)) cfg = HGEMM_SM100_CFG_SPLITK_128x128;
+            }
         }
     }
     if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x256;
@@ -528,7 +569,7 @@ int launch_copy(const __half* src, int64_t ld_src, __half* dst, int64_t ld_dst, 
 // Launches the resolved configuration on operands that TMA can describe
 // (or, for the generic configuration, on any operands).
 int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceInfo& dev, int devid,
-             cudaStream_t stream, uint8_t* sk_region) {
+             cudaStream_t stream, uint8_t* region, size_t region_bytes) {
     int rc = HGEMM_SM100_OK;
     GemmParams p{};
     p.a = static_cast<const __half*>(a.a);
@@ -553,13 +594,17 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
     std::memset(&map_c, 0, sizeof(map_c));
     // TMA-store epilogue (persistent and pair kernels): FP16 C whose base and
     // pitch TMA can describe; boxes of 32 rows x 64 columns.
-    auto prepare_store = [&]() -> int {
+    // Swapped tile kernels store [kChunk rows x 32 columns] boxes, unswizzled.
+    auto prepare_store = [&](uint32_t box_cols = 64, uint32_t box_rows = 32, bool swizzle = true) -> int {
         if (!p.vec_ok || p.out_f32) return HGEMM_SM100_OK;
         const int r = tensor_map(&map_c, a.c, static_cast<uint64_t>(a.n), static_cast<uint64_t>(a.m),
-                                 static_cast<uint64_t>(a.ldc), 64, 32);
+                                 static_cast<uint64_t>(a.ldc), box_cols, box_rows, swizzle);
         if (r == HGEMM_SM100_OK) p.tma_store = 1;
         return r;
     };
+    // Split-K partial exchange through the workspace when the caller gave one.
+    if (split > 1 && region != nullptr && region_bytes >= exchange_bytes(cfg, a.m, a.n, split))
+        p.partials = reinterpret_cast<float*>(region);
     const uint64_t M = a.m, N = a.n, K = a.k;
 
     switch (cfg) {
@@ -597,6 +642,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             const int bn = wide ? 256 : 128;
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if (split == 1 && (rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, bn)),
                             static_cast<unsigned>(split));
@@ -608,6 +654,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                 HGEMM_SM100_OK)
                 return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if (split == 1 && (rc = prepare_store(32, sc.bnm >= 32 ? 32 : 16, false)) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(*sc.k, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
                             static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
@@ -629,9 +676,9 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             p.streamk = sp.streamk;
             p.group_m = sp.swap ? 1 : 16;
             if (sp.streamk) {
-                if (sk_region == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
-                p.partials = reinterpret_cast<float*>(sk_region);
-                p.flags = reinterpret_cast<unsigned long long*>(sk_region +
+                if (region == nullptr || region_bytes < sp.bytes) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+                p.partials = reinterpret_cast<float*>(region);
+                p.flags = reinterpret_cast<unsigned long long*>(region +
                                                                 static_cast<size_t>(sp.grid) * sp.slot_bytes);
                 p.epoch = next_epoch();
             }
@@ -639,6 +686,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                           sp.streamk != 0);
         }
         case HGEMM_SM100_CFG_GENERIC_128x128: {
+            if (split == 1 && (rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(g_generic_128, devid)) != HGEMM_SM100_OK) return rc;
             const dim3 grid(static_cast<unsigned>(cdiv(a.m, 128)), static_cast<unsigned>(cdiv(a.n, 128)),
                             static_cast<unsigned>(split));
@@ -677,14 +725,21 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     rc = resolve(*args, *dev, &cfg, &split);
     if (rc != HGEMM_SM100_OK) return rc;
 
-    // Workspace layout: [staging buffers][stream-K partial slots + flags].
+    // Workspace layout: [staging buffers][kernel region: stream-K partial
+    // slots + flags, or split-K exchange slots].
     const Staging st = plan_staging(*args);
     const bool staged = cfg != HGEMM_SM100_CFG_GENERIC_128x128 && staging_usable(*args, st);
     uint8_t* ws = static_cast<uint8_t*>(args->workspace);
-    uint8_t* sk_region = nullptr;
-    if (is_streamk(cfg) && ws != nullptr) sk_region = ws + align_up(staged ? st.total : 0, kStageAlign);
+    uint8_t* region = nullptr;
+    size_t region_bytes = 0;
+    const size_t region_off = align_up(staged ? st.total : 0, kStageAlign);
+    if (ws != nullptr && reinterpret_cast<uintptr_t>(ws) % kStageAlign == 0 && args->workspace_bytes > region_off &&
+        region_need(cfg, split, args->m, args->n, args->k, dev->sms) > 0) {
+        region = ws + region_off;
+        region_bytes = static_cast<size_t>(args->workspace_bytes) - region_off;
+    }
 
-    if (!staged) return run_core(*args, cfg, split, *dev, devid, stream, sk_region);
+    if (!staged) return run_core(*args, cfg, split, *dev, devid, stream, region, region_bytes);
 
     // Stage, run on the staged operands, copy a staged C back.
     HgemmSm100Args s = *args;
@@ -710,7 +765,7 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     }
     s.config = cfg;
     s.split_k = split;
-    if ((rc = run_core(s, cfg, split, *dev, devid, stream, sk_region)) != HGEMM_SM100_OK) return rc;
+    if ((rc = run_core(s, cfg, split, *dev, devid, stream, region, region_bytes)) != HGEMM_SM100_OK) return rc;
     if (st.c)
         return launch_copy(static_cast<const __half*>(s.c), st.ldc, static_cast<__half*>(args->c), args->ldc,
                            args->m, args->n, false, dev->sms, stream);
@@ -726,10 +781,8 @@ extern "C" size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args) {
     int32_t cfg = 0, split = 0;
     resolve_cfg(*args, *dev, true, &cfg, &split);
     if (cfg == HGEMM_SM100_CFG_GENERIC_128x128) return 0;
-    if (is_streamk(cfg)) {
-        const StreamKPlan sp = plan_streamk(cfg, args->m, args->n, args->k, dev->sms);
-        if (sp.bytes > 0) total = align_up(total, kStageAlign) + sp.bytes;
-    }
+    const size_t region = region_need(cfg, split, args->m, args->n, args->k, dev->sms);
+    if (region > 0) total = align_up(total, kStageAlign) + region;
     return total;
 }
 
@@ -748,10 +801,25 @@ extern "C" const char* hgemm_sm100_config_name(int32_t config) {
 extern "C" int32_t hgemm_sm100_num_configs(void) { return HGEMM_SM100_CFG_COUNT; }
 
 extern "C" size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k) {
-    if (!is_streamk(config) || m <= 0 || n <= 0 || k <= 0) return 0;
+    if (m <= 0 || n <= 0 || k <= 0 || config < 0 || config >= HGEMM_SM100_CFG_COUNT) return 0;
+    if (!is_streamk(config) && !is_tile_cfg(config)) return 0;
     const DeviceInfo* dev = nullptr;
     if (device_info(&dev) != HGEMM_SM100_OK) return 0;
-    return plan_streamk(config, m, n, k, dev->sms).bytes;
+    if (is_streamk(config)) return plan_streamk(config, m, n, k, dev->sms).bytes;
+    // The split the tile configuration chooses for aligned operands.
+    HgemmSm100Args a{};
+    static const uint8_t dummy[16] = {};
+    a.a = a.b = dummy;
+    a.c = const_cast<uint8_t*>(dummy);
+    a.m = m;
+    a.n = n;
+    a.k = k;
+    a.lda = align_up(static_cast<size_t>(k), 8);
+    a.ldb = a.ldc = align_up(static_cast<size_t>(n), 8);
+    a.config = config;
+    int32_t cfg = 0, split = 0;
+    if (resolve_cfg(a, *dev, true, &cfg, &split) != HGEMM_SM100_OK) return 0;
+    return exchange_bytes(cfg, m, n, split);
 }
 
 extern "C" const char* hgemm_sm100_status_string(int status) {
@@ -835,5 +903,6 @@ extern "C" int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* 
     if (sp.bytes > HGEMM_SM100_STATIC_SCRATCH_BYTES) return HGEMM_SM100_ERR_SCRATCH_LIMIT;
     uint8_t* scratch = nullptr;
     if (sp.bytes > 0 && (rc = static_scratch(devid, &scratch)) != HGEMM_SM100_OK) return rc;
-    return run_core(*args, cfg, 1, *dev, devid, static_cast<cudaStream_t>(stream_ptr), scratch);
+    return run_core(*args, cfg, 1, *dev, devid, static_cast<cudaStream_t>(stream_ptr), scratch,
+                    scratch != nullptr ? HGEMM_SM100_STATIC_SCRATCH_BYTES : 0);
 }

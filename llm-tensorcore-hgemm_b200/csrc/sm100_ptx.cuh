@@ -196,6 +196,25 @@ __device__ __forceinline__ void fence_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's generic-proxy and async-proxy (bulk copy) accesses to
+// global memory.
+__device__ __forceinline__ void fence_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Untiled bulk copy this CTA's shared memory -> global (addresses 16-byte
+// aligned, size a multiple of 16), tracked by the bulk async-group.
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
+                 ::"l"(reinterpret_cast<uint64_t>(dst)), "r"(smem_addr(src)), "r"(bytes)
+                 : "memory");
+}
+
+// Barrier among the 128 threads of warps 0-3 (named barrier 1).
+__device__ __forceinline__ void epilogue_bar_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
 // --------------------------------------------------------------- tcgen05 ---
 
 // Allocates `ncols` TMEM columns (power of two, 32..512); must be executed by

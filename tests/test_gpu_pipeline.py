@@ -34,13 +34,14 @@ def _cuda():
     require_cuda()
 
 
-def run_capi(a, b, out, config, split_k=0, flags=0):
-    """Calls the C ABI with the workspace it asks for (staging, stream-K)."""
+def run_capi(a, b, out, config, split_k=0, flags=0, workspace=True):
+    """Calls the C ABI with the workspace it asks for (staging, stream-K,
+    split-K exchange), or with none."""
     m, k = a.shape
     n = b.shape[1]
     args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k,
                           config=config, split_k=split_k, flags=flags)
-    need = capi.workspace_size(args)
+    need = capi.workspace_size(args) if workspace else 0
     ws = torch.empty(max(need, 1), device="cuda", dtype=torch.uint8)
     if need:
         args.workspace, args.workspace_bytes = ws.data_ptr(), need
@@ -68,19 +69,40 @@ def test_stage_markers_every_ring_depth(impl, kblocks, mn):
     torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
 
 
-@pytest.mark.parametrize("config", ["tc_splitk_128x128", "tc_splitk_128x256", "tc_swapab",
-                                    "tc_generic_128x128"])
+SPLIT_CONFIGS = ["tc_splitk_128x128", "tc_splitk_128x256", "tc_swapab", "tc_generic_128x128"]
+
+
+@pytest.mark.parametrize("workspace", [True, False], ids=["l2_exchange", "dsmem_push"])
+@pytest.mark.parametrize("config", SPLIT_CONFIGS)
 @pytest.mark.parametrize("split", [1, 2, 3, 4, 5, 8, 16])
-def test_explicit_split_k(config, split):
+def test_explicit_split_k(config, split, workspace):
     m, n, k = (48, 384, 64 * 17) if config == "tc_swapab" else (200, 260, 64 * 17)
     a, b, value = oracle.stage_marker_inputs(m, n, k, 64, device="cuda")
     out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
-    run_capi(a, b, out, CONFIG_IDS[config], split_k=split)
+    run_capi(a, b, out, CONFIG_IDS[config], split_k=split, workspace=workspace)
     torch.testing.assert_close(out, torch.full_like(out, value), rtol=0, atol=0)
     a, b = seeded_inputs(m, n, k + 5)
     out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
-    run_capi(a, b, out, CONFIG_IDS[config], split_k=split)
+    run_capi(a, b, out, CONFIG_IDS[config], split_k=split, workspace=workspace)
     assert_gate(out, a, b)
+
+
+@pytest.mark.parametrize("out_f32", [False, True], ids=["fp16", "fp32"])
+@pytest.mark.parametrize("config", SPLIT_CONFIGS)
+@pytest.mark.parametrize("split", [2, 3, 7, 16])
+def test_split_transports_bitwise_equal(config, split, out_f32):
+    """Both partial-tile transports sum the same FP32 partials in the same
+    rank order: identical bits."""
+    m, n, k = (40, 520, 64 * 19) if config == "tc_swapab" else (260, 520, 64 * 19)
+    a, b = seeded_inputs(m, n, k)
+    dtype = torch.float32 if out_f32 else torch.float16
+    flags = capi.FLAG_OUT_F32 if out_f32 else 0
+    via_l2 = torch.full((m, n), float("nan"), device="cuda", dtype=dtype)
+    via_dsmem = torch.full((m, n), float("nan"), device="cuda", dtype=dtype)
+    run_capi(a, b, via_l2, CONFIG_IDS[config], split_k=split, flags=flags, workspace=True)
+    run_capi(a, b, via_dsmem, CONFIG_IDS[config], split_k=split, flags=flags, workspace=False)
+    assert torch.equal(via_l2, via_dsmem)
+    assert_gate(via_l2.half() if out_f32 else via_l2, a, b)
 
 
 @pytest.mark.parametrize("config", list(CONFIG_IDS))

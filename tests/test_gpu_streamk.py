@@ -106,7 +106,8 @@ def test_streamk_graph_replay(shape):
 
 @pytest.mark.parametrize("shape,expected", [
     ((1, 151936, 2560), "tc_streamk_swapab"), ((16, 4096, 2560), "tc_swapab"),
-    ((2048, 2560, 4096), "tc_streamk_128x256"), ((512, 4096, 2560), "tc_splitk_128x256"),
+    ((2048, 2560, 4096), "tc_streamk_128x256"), ((512, 2560, 4096), "tc_splitk_128x256"),
+    ((512, 4096, 2560), "tc_splitk_128x128"), ((512, 1024, 2560), "tc_splitk_128x128"),
     ((8192, 8192, 1024), "tc_persistent_128x256")])
 def test_auto_picks_streamk_when_tiles_fill_the_sms(shape, expected):
     a, b = seeded_inputs(*shape)
