@@ -66,7 +66,11 @@ enum {
                                               C^T = B^T A^T, M <= 128           */
     HGEMM_SM100_CFG_PAIR_256x128 = 10,     /* "tc_pair_256x128": CTA pair, 256 x 128
                                               tiles (one wave for mid-size M)   */
-    HGEMM_SM100_CFG_COUNT = 11
+    HGEMM_SM100_CFG_PAIR_128x256 = 11,     /* "tc_pair_128x256": CTA pair, 128 x 256
+                                              tiles, 64 rows per CTA            */
+    HGEMM_SM100_CFG_PAIR_128x128 = 12,     /* "tc_pair_128x128": CTA pair, 128 x 128
+                                              tiles, 64 rows per CTA            */
+    HGEMM_SM100_CFG_COUNT = 13
 };
 
 /* Flags. */

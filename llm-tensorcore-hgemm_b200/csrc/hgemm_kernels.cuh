@@ -288,12 +288,15 @@ __device__ __forceinline__ uint64_t mnmaj_desc(uint32_t tile, int kk) {
 
 // Waits for the last armed phase of every used stage's full barrier, so that
 // no TMA write into this CTA's shared memory is still in flight at exit.
-template <int kStages>
-__device__ __forceinline__ void drain_tma(uint64_t* full, uint32_t issued) {
-    const uint32_t used = issued < kStages ? issued : kStages;
-    for (uint32_t s = 0; s < used; ++s) {
-        const uint32_t arms = issued / kStages + (s < issued % kStages ? 1u : 0u);
-        mbar_wait_drain(&full[s], (arms - 1u) & 1u, kDrainLimitNs);
+// A producer that owns every kStep-th stage from `which` on (kStages a
+// multiple of kStep) and armed `issued` loads in order drains its own stages.
+template <int kStages, int kStep = 1>
+__device__ __forceinline__ void drain_tma(uint64_t* full, uint32_t issued, uint32_t which = 0) {
+    constexpr uint32_t kOwn = kStages / kStep;
+    const uint32_t used = issued < kOwn ? issued : kOwn;
+    for (uint32_t t = 0; t < used; ++t) {
+        const uint32_t arms = issued / kOwn + (t < issued % kOwn ? 1u : 0u);
+        mbar_wait_drain(&full[which + kStep * t], (arms - 1u) & 1u, kDrainLimitNs);
     }
 }
 
@@ -312,10 +315,9 @@ struct TileCfg {
     // owns: [s][local row][kBNm + 4] or, swapped, [s][col][local row] (the
     // output's contiguous dimension contiguous, quads 16-byte aligned). Rows
     // per rank <= 4 * ceil(32 / split); over split 2..16,
-    // split * 4 * ceil(32 / split) <= 180. Small swapped tiles get a buffer of
-    // their own (no overlap with the stage ring); the others reuse the ring
-    // once every CTA's MMAs are done.
-    static constexpr bool kRecvOwn = kSwap && kBNm <= 32;
+    // split * 4 * ceil(32 / split) <= 180. The buffer reuses the stage ring
+    // once every CTA's MMAs are done (the ring is deep for narrow tiles).
+    static constexpr bool kRecvOwn = false;
     static constexpr uint32_t kRecvBytes = kSwap ? 180u * kBNm * 4u : 180u * (kBNm + 4) * 4u;
     static constexpr uint32_t kRecvOff = kRecvOwn ? kStages * kStageBytes : 0u;
     // Workspace exchange: one FP32 tile per CTA, staged in the stage ring.
@@ -326,15 +328,44 @@ struct TileCfg {
         kRecvOwn ? kStages * kStageBytes + kRecvBytes : cmax(kStages * kStageBytes, kRecvBytes);
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
-    static constexpr uint32_t kTmemCols = tmem_cols_for(kBNm);
+    // Two TMA producers and two MMA issuers with an accumulator each for
+    // tiles of at most 128 columns fed by TMA (see the kernel); one of each
+    // otherwise. Each producer owns the stages of one parity.
+    static constexpr bool kDual = kTma && kBNm <= 128;
+    static_assert(!kDual || kStages % 2 == 0, "dual producers own alternate stages");
+    static constexpr uint32_t kTmemCols = tmem_cols_for(kDual ? 2 * kBNm : kBNm);
     static constexpr uint32_t kIdesc = make_idesc_f16(kMmaM, kBNm, kSwap, !kSwap);
     static constexpr int kChunk = kBNm >= 32 ? 32 : 16;     // columns per tcgen05.ld
     static_assert(kKRows % 8 == 0, "K-major tile rows must fill 8-row swizzle atoms");
     static_assert(kMNCols % 64 == 0, "MN-major tile must be whole 64-wide chunks");
     static_assert(kBNm % 16 == 0 && kBNm >= 16 && kBNm <= 256, "UMMA N for M=128");
-    static_assert(2 * kStages + 2 <= 30, "barrier area");
+    static_assert(2 * kStages + 4 <= 30, "barrier area");
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
+
+// Loads kCnt accumulator columns at TMEM address t (the warp's lane base
+// included); with `two`, adds the second accumulator at t + off. Warp-uniform.
+template <int kCnt>
+__device__ __forceinline__ void tmem_ld_acc(uint32_t t, uint32_t off, bool two, uint32_t (&v)[kCnt]) {
+    if constexpr (kCnt == 32) {
+        tmem_ld_32x32b_x32(t, v);
+    } else {
+        tmem_ld_32x32b_x16(t, v);
+    }
+    if (two) {
+        uint32_t w[kCnt];
+        if constexpr (kCnt == 32) {
+            tmem_ld_32x32b_x32(t + off, w);
+        } else {
+            tmem_ld_32x32b_x16(t + off, w);
+        }
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < kCnt; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w[j]));
+    } else {
+        tmem_wait_ld();
+    }
+}
 
 // Split-K reduction of the rows this CTA owns (first .. first + nrows - 1 of
 // the accumulator tile) from the receive buffer, summed over ranks
@@ -413,8 +444,9 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
     uint64_t* empty = full + kStages;
     uint64_t* tfull = empty + kStages;
-    uint64_t* drain = tfull + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* drain = tfull + 1;           // [2], one per MMA issuer
+    uint64_t* xfer = drain + 2;            // split-K partial rows landed (workspace exchange)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfer + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const uint32_t warp = warp_index();
@@ -425,8 +457,10 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
             mbar_init(&full[s], kTma ? 1u : 128u);
             mbar_init(&empty[s], 1u);
         }
-        mbar_init(tfull, 1u);
-        mbar_init(drain, 1u);
+        mbar_init(tfull, Cfg::kDual ? 2u : 1u);
+        mbar_init(&drain[0], 1u);
+        mbar_init(&drain[1], 1u);
+        mbar_init(xfer, 1u);
         *abort_flag = 0;
         mbar_init_fence();
         if (kTma) {
@@ -453,12 +487,21 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     const int kb0 = static_cast<int>(blockIdx.z) * nkb / split;
     const int kb1 = (static_cast<int>(blockIdx.z) + 1) * nkb / split;
 
-    // ---------------------------------------------------------- producer --
+    // --------------------------------------------------------- producers --
+    // A producer thread's barrier waits and copy issues take a few hundred
+    // cycles per K block; with narrow tiles that is more than the MMAs, so
+    // kDual tiles use two producers: lane 0 of warp 4 loads the even K blocks
+    // (even stages), lane 0 of warp 2 (idle until the epilogue) the odd ones.
     if (kTma) {
-        if (warp == 4 && lane == 0) {
-            uint32_t stage = 0, phase = 0, issued = 0;
+        if (lane == 0 && (warp == 4 || (Cfg::kDual && warp == 2))) {
+            const int which = warp == 4 ? 0 : 1;
+            constexpr int kStep = Cfg::kDual ? 2 : 1;
+            uint32_t issued = 0;
             bool ok = true;
-            for (int kb = kb0; kb < kb1; ++kb) {
+            for (int kb = kb0 + which; kb < kb1; kb += kStep) {
+                const int i = kb - kb0;
+                const uint32_t stage = static_cast<uint32_t>(i % kStages);
+                const uint32_t phase = static_cast<uint32_t>(i / kStages) & 1u;
                 if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
                 uint8_t* s_k = smem + stage * Cfg::kStageBytes;
                 uint8_t* s_mn = s_k + Cfg::kKBytes;
@@ -470,9 +513,8 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
                     tma_load_2d(s_mn + j * kChunkBytes, &tm_mn, &full[stage], mn_cols0 + 64 * j,
                                 kb * kBlockK);
                 ++issued;
-                if (++stage == kStages) { stage = 0; phase ^= 1u; }
             }
-            if (!ok || *abort_flag) drain_tma<kStages>(full, issued);
+            if (!ok || *abort_flag) drain_tma<kStages, kStep>(full, issued, static_cast<uint32_t>(which));
         }
     } else if (warp < 4) {
         const int tid = threadIdx.x;
@@ -489,11 +531,23 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
         }
     }
 
-    // ------------------------------------------------------- MMA issuer --
-    if (warp == 5 && lane == 0) {
-        uint32_t stage = 0, phase = 0;
-        bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb) {
+    // ------------------------------------------------------ MMA issuers --
+    // One thread issues a K block's MMAs and commits the block's stage. An
+    // issuer's barrier wait leaves the tensor pipe idle for a few hundred
+    // cycles, which the 64-cycle MMAs of a narrow tile cannot cover, so tiles
+    // of at most 128 columns use two issuers: lane 0 of warp 5 takes the even
+    // K blocks into accumulator 0, lane 0 of warp 3 (idle until the epilogue)
+    // the odd ones into accumulator 1, and each fills the other's gaps. The
+    // epilogue adds the two accumulators (fixed order: deterministic).
+    if (lane == 0 && (warp == 5 || (Cfg::kDual && warp == 3))) {
+        const int which = warp == 5 ? 0 : 1;
+        constexpr int kStep = Cfg::kDual ? 2 : 1;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(which * kBNm);
+        bool ok = true, first = true;
+        for (int kb = kb0 + which; kb < kb1; kb += kStep) {
+            const int i = kb - kb0;
+            const uint32_t stage = static_cast<uint32_t>(i % kStages);
+            const uint32_t phase = static_cast<uint32_t>(i / kStages) & 1u;
             if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
             tc_fence_after_sync();
             const uint32_t s_k = smem_addr(smem + stage * Cfg::kStageBytes);
@@ -502,20 +556,21 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
             for (int kk = 0; kk < kBlockK / 16; ++kk) {
                 const uint64_t dk = kmaj_desc(s_k, kk);
                 const uint64_t dmn = mnmaj_desc(s_mn, kk);
-                tc_mma_f16(tmem_base, kSwap ? dmn : dk, kSwap ? dk : dmn, Cfg::kIdesc,
-                           (kb > kb0 || kk > 0) ? 1u : 0u);
+                tc_mma_f16(d, kSwap ? dmn : dk, kSwap ? dk : dmn, Cfg::kIdesc, (!first || kk > 0) ? 1u : 0u);
             }
+            first = false;
             tc_commit(&empty[stage]);
-            if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
         if (ok) {
             tc_commit(tfull);
         } else {
-            tc_commit(drain);
-            mbar_wait_drain(drain, 0, kDrainLimitNs);
+            tc_commit(&drain[which]);
+            mbar_wait_drain(&drain[which], 0, kDrainLimitNs);
         }
     }
     __syncwarp();
+    // Accumulator 1 holds data only when its issuer had a K block.
+    const bool two = Cfg::kDual && kb1 - kb0 >= 2;
 
     // --------------------------------------------------------- epilogue --
     // Without a split the accumulator goes to C: through per-warp shared-memory
@@ -565,9 +620,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
 #pragma unroll 1
                     for (int c = 0; c < kBNm; c += Cfg::kChunk) {
                         uint32_t v[Cfg::kChunk];
-                        if constexpr (Cfg::kChunk == 32) tmem_ld_32x32b_x32(t_row + c, v);
-                        else tmem_ld_32x32b_x16(t_row + c, v);
-                        tmem_wait_ld();
+                        tmem_ld_acc<Cfg::kChunk>(t_row + c, kBNm, two, v);
                         store_box_tma_t<Cfg::kChunk>(&tm_c, boxes + buf * 2048u, lane, v,
                                                      acc_row0 + static_cast<int>(warp) * 32, acc_col0 + c);
                         buf ^= 1u;
@@ -576,9 +629,8 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
 #pragma unroll 1
                     for (int c = 0; c < kBNm; c += 64) {
                         uint32_t v0[32], v1[32];
-                        tmem_ld_32x32b_x32(t_row + c, v0);
-                        tmem_ld_32x32b_x32(t_row + c + 32, v1);
-                        tmem_wait_ld();
+                        tmem_ld_acc<32>(t_row + c, kBNm, two, v0);
+                        tmem_ld_acc<32>(t_row + c + 32, kBNm, two, v1);
                         store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, acc_col0 + c,
                                       acc_row0 + static_cast<int>(warp) * 32);
                         buf ^= 1u;
@@ -592,12 +644,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
 #pragma unroll 1
                 for (int c = 0; c < kBNm; c += Cfg::kChunk) {
                     uint32_t v[Cfg::kChunk];
-                    if constexpr (Cfg::kChunk == 32) {
-                        tmem_ld_32x32b_x32(t_row + c, v);
-                    } else {
-                        tmem_ld_32x32b_x16(t_row + c, v);
-                    }
-                    tmem_wait_ld();
+                    tmem_ld_acc<Cfg::kChunk>(t_row + c, kBNm, two, v);
                     if (via_l2) {
                         if constexpr (kSwap) {
                             // Owner blocks [col][local row], block o at kBNm * o_first.
@@ -681,17 +728,17 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
             fence_async_global();
             const uint32_t row_floats = kSwap ? kBNm : kBNm + 4;   // floats per owned row
             const uint32_t bytes = static_cast<uint32_t>(nrows) * row_floats * 4u;
-            mbar_arrive_expect_tx(tfull, bytes * static_cast<uint32_t>(split));
+            mbar_arrive_expect_tx(xfer, bytes * static_cast<uint32_t>(split));
             for (int s2 = 0; s2 < split; ++s2) {
                 const float* src = p.partials + (slot0 + zstride * s2) * Cfg::kSlotFloats +
                                    static_cast<size_t>(first) * row_floats;
-                bulk_load(recv + static_cast<size_t>(s2) * nrows_max * row_floats, src, bytes, tfull);
+                bulk_load(recv + static_cast<size_t>(s2) * nrows_max * row_floats, src, bytes, xfer);
             }
         }
         // Every thread of the CTA reduces; the wait is bounded like any other.
-        ok = go && mbar_wait(tfull, 1, wc);
+        ok = go && mbar_wait(xfer, 0, wc);
         // After a timeout, the issuing thread lets its copies land (bounded).
-        if (go && !ok && threadIdx.x == 0) mbar_wait_drain(tfull, 1, kDrainLimitNs);
+        if (go && !ok && threadIdx.x == 0) mbar_wait_drain(xfer, 0, kDrainLimitNs);
         if (ok) reduce_owned_rows<kBNm, kSwap>(p, recv, split, nrows, nrows_max, sw_stride, first, acc_row0, acc_col0);
     } else if (split_k) {
         cluster_sync();
@@ -885,40 +932,50 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
 
 // ============================================== CTA-pair persistent kernel ====
 //
-// 256 x kTileN output tiles (kTileN = 256 or 128) per cluster of two CTAs
-// (cta_group::2). CTA r of the pair TMA-loads rows 128r .. 128r+127 of the A
-// tile and the r-th kTileN/2 columns of the B tile into its own shared
-// memory; the even CTA's single MMA thread issues M=256, N=kTileN MMAs that
-// read both CTAs' tiles, and each CTA's TMEM receives its own 128 accumulator
-// rows (two kTileN-column buffers).
+// kTileM x kTileN output tiles (kTileM = 256 or 128, kTileN = 256 or 128) per
+// cluster of two CTAs (cta_group::2). CTA r of the pair TMA-loads the r-th
+// kTileM/2 rows of the A tile and the r-th kTileN/2 columns of the B tile
+// into its own shared memory; the even CTA's single MMA thread issues
+// M=kTileM, N=kTileN MMAs that read both CTAs' tiles, and each CTA's TMEM
+// receives the accumulator of its own kTileM/2 rows (two buffers). With
+// 128 rows per CTA, row i sits in TMEM lane i. With 64 rows per CTA the
+// accumulator is folded: lanes 0-63 hold rows 0-63 of columns 0 .. kTileN/2-1
+// and lanes 64-127 the same rows of columns kTileN/2 .. kTileN-1, in
+// kTileN/2 TMEM columns. 64-row tiles halve the A bytes each SM's tensor
+// core reads per MMA (the per-MMA cost at N <= 256 is set by A rows), so
+// they keep full efficiency at half the M granularity.
 // Both CTAs' loads complete their bytes on the even CTA's "stage full"
 // barrier (armed once with both CTAs' bytes); the MMA thread commits "stage
 // empty" and "accumulator full" to the barriers of both CTAs; one lane per
 // epilogue warp of either CTA arrives on the even CTA's "accumulator empty".
 
-template <int kTileNT, int kStages>
+template <int kTileMT, int kTileNT, int kStages>
 struct PairCfg {
-    static constexpr int kTileM = 256, kTileN = kTileNT;   // pair tile; each CTA: 128 x kTileN
-    static constexpr int kHalfN = kTileN / 2;              // B columns each CTA loads
-    static constexpr uint32_t kABytes = 128u * 128u;        // 128 rows x 64 halves
-    static constexpr uint32_t kBBytes = kHalfN * 128u;      // 64 k-rows x kHalfN halves
+    static constexpr int kTileM = kTileMT, kTileN = kTileNT;   // pair tile
+    static constexpr int kRows = kTileM / 2;                   // A rows (output rows) per CTA
+    static constexpr int kHalfN = kTileN / 2;                  // B columns each CTA loads
+    static constexpr bool kFolded = kRows == 64;               // 64-row accumulator layout
+    static constexpr uint32_t kAccCols = kFolded ? kTileN / 2 : kTileN;   // TMEM columns per buffer
+    static constexpr uint32_t kABytes = kRows * 128u;           // kRows rows x 64 halves
+    static constexpr uint32_t kBBytes = kHalfN * 128u;          // 64 k-rows x kHalfN halves
     static constexpr uint32_t kStageBytes = kABytes + kBBytes;
     static constexpr uint32_t kEpiBytes = 4u * 2u * 4096u;   // 4 warps x 2 boxes of 32 x 64 halves
     static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
-    static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kTileN);   // 2 accumulators
-    static constexpr uint32_t kIdesc = make_idesc_f16(256, kTileN, false, true);
+    static constexpr uint32_t kTmemCols = tmem_cols_for(2 * kAccCols);   // 2 accumulators
+    static constexpr uint32_t kIdesc = make_idesc_f16(kTileM, kTileN, false, true);
     static_assert(kTileN == 128 || kTileN == 256, "pair tile width");
+    static_assert(kTileM == 128 || kTileM == 256, "pair tile height");
     static_assert(2 * kStages + 5 <= 30, "barrier area");
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
-template <int kTileNT, int kStages>
+template <int kTileMT, int kTileNT, int kStages>
 __global__ void __launch_bounds__(kThreads, 1)
 hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                   const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
-    using Cfg = PairCfg<kTileNT, kStages>;
+    using Cfg = PairCfg<kTileMT, kTileNT, kStages>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = align_1024(smem_raw);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);   // even CTA
@@ -973,7 +1030,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             for (int t = pair; t < num_tiles && ok; t += npairs) {
                 int tm, tn;
                 tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-                const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * 128;
+                const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kRows;
                 const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
@@ -1002,7 +1059,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
                 if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, wc)) { ok = false; break; }
                 tc_fence_after_sync();
-                const uint32_t d = tmem_base + acc * Cfg::kTileN;
+                const uint32_t d = tmem_base + acc * Cfg::kAccCols;
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
                     tc_fence_after_sync();
@@ -1040,25 +1097,30 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             tc_fence_after_sync();
             int tm, tn;
             tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
-            const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * 128 + warp * 32;
-            const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kTileN;
+            // Warp w: its 32 TMEM lanes are rows row0 .. row0 + 31 of columns
+            // col0 .. col0 + kAccCols - 1 (folded layout: warps 2, 3 hold the
+            // right half of the columns of the rows of warps 0, 1).
+            const int wrow = Cfg::kFolded ? static_cast<int>(warp & 1u) * 32 : static_cast<int>(warp) * 32;
+            const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kRows + wrow;
+            const int col0 = tn * Cfg::kTileN + (Cfg::kFolded ? static_cast<int>(warp >> 1) * (Cfg::kTileN / 2) : 0);
+            const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kAccCols;
             if (p.tma_store) {
 #pragma unroll 1
-                for (int c = 0; c < Cfg::kTileN; c += 64) {
+                for (int c = 0; c < static_cast<int>(Cfg::kAccCols); c += 64) {
                     uint32_t v0[32], v1[32];
                     tmem_ld_32x32b_x32(t_acc + c, v0);
                     tmem_ld_32x32b_x32(t_acc + c + 32, v1);
                     tmem_wait_ld();
-                    store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, tn * Cfg::kTileN + c, row0);
+                    store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, col0 + c, row0);
                     buf ^= 1u;
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < Cfg::kTileN; c += 32) {
+                for (int c = 0; c < static_cast<int>(Cfg::kAccCols); c += 32) {
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(t_acc + c, v);
                     tmem_wait_ld();
-                    store_row_segment<32>(p, row0 + static_cast<int>(lane), tn * Cfg::kTileN + c, v);
+                    store_row_segment<32>(p, row0 + static_cast<int>(lane), col0 + c, v);
                 }
             }
             tc_fence_before_sync();

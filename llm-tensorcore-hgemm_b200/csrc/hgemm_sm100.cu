@@ -40,6 +40,8 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_streamk_128x256",
     "tc_streamk_swapab",
     "tc_pair_256x128",
+    "tc_pair_128x256",
+    "tc_pair_128x128",
 };
 
 // ------------------------------------------------------ device properties --
@@ -179,9 +181,9 @@ int prepare_kernel(KernelEntry& k, int dev) {
         reinterpret_cast<const void*>(&hgemm_tile_kernel<BN, SWAP, TMA, ST>),              \
             TileCfg<BN, SWAP, TMA, ST>::kSmemBytes                                         \
     }
-#define HG_PAIR(BN, ST)                                                                   \
-    KernelEntry {                                                                          \
-        reinterpret_cast<const void*>(&hgemm_pair_kernel<BN, ST>), PairCfg<BN, ST>::kSmemBytes \
+#define HG_PAIR(BM, BN, ST)                                                                        \
+    KernelEntry {                                                                                   \
+        reinterpret_cast<const void*>(&hgemm_pair_kernel<BM, BN, ST>), PairCfg<BM, BN, ST>::kSmemBytes \
     }
 #define HG_STREAMK(BN, SWAP, ST)                                                          \
     KernelEntry {                                                                          \
@@ -194,8 +196,10 @@ int prepare_kernel(KernelEntry& k, int dev) {
             PersistCfg<BN, ST>::kSmemBytes                                                 \
     }
 
-KernelEntry g_pair_256 = HG_PAIR(256, 6);
-KernelEntry g_pair_128 = HG_PAIR(128, 8);
+KernelEntry g_pair_256 = HG_PAIR(256, 256, 6);
+KernelEntry g_pair_128 = HG_PAIR(256, 128, 8);
+KernelEntry g_pair_m128_256 = HG_PAIR(128, 256, 8);
+KernelEntry g_pair_m128_128 = HG_PAIR(128, 128, 12);
 KernelEntry g_sk_256 = HG_STREAMK(256, false, 4);
 KernelEntry g_sk_swap_16 = HG_STREAMK(16, true, 10);
 KernelEntry g_sk_swap_32 = HG_STREAMK(32, true, 9);
@@ -209,10 +213,10 @@ KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
 // Swap-AB tiles for M <= 128 use at most ~110 KB of shared memory so that two
 // CTAs (of different clusters) share an SM; their TMEM (<= 128 columns
 // each) then fits twice into the 512 columns.
-KernelEntry g_swap_16 = HG_TILE(16, true, true, 5);
-KernelEntry g_swap_32 = HG_TILE(32, true, true, 4);
-KernelEntry g_swap_64 = HG_TILE(64, true, true, 9);
-KernelEntry g_swap_128 = HG_TILE(128, true, true, 7);
+KernelEntry g_swap_16 = HG_TILE(16, true, true, 12);
+KernelEntry g_swap_32 = HG_TILE(32, true, true, 10);
+KernelEntry g_swap_64 = HG_TILE(64, true, true, 8);
+KernelEntry g_swap_128 = HG_TILE(128, true, true, 6);
 KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
 
 struct SwapChoice {
@@ -221,8 +225,8 @@ struct SwapChoice {
     int per_sm;   // CTAs that fit on one SM
 };
 SwapChoice swap_choice(int64_t m) {
-    if (m <= 16) return {16, &g_swap_16, 2};
-    if (m <= 32) return {32, &g_swap_32, 2};
+    if (m <= 16) return {16, &g_swap_16, 1};
+    if (m <= 32) return {32, &g_swap_32, 1};
     if (m <= 64) return {64, &g_swap_64, 1};
     if (m <= 128) return {128, &g_swap_128, 1};
     return {256, &g_swap_256, 1};
@@ -622,14 +626,21 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             return launch(k, dim3(static_cast<unsigned>(grid), 1, 1), 1, map_k, map_mn, map_c, p, stream);
         }
         case HGEMM_SM100_CFG_PAIR_256x256:
-        case HGEMM_SM100_CFG_PAIR_256x128: {
-            const bool wide = cfg == HGEMM_SM100_CFG_PAIR_256x256;
-            KernelEntry& k = wide ? g_pair_256 : g_pair_128;
-            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+        case HGEMM_SM100_CFG_PAIR_256x128:
+        case HGEMM_SM100_CFG_PAIR_128x256:
+        case HGEMM_SM100_CFG_PAIR_128x128: {
+            const int tm = (cfg == HGEMM_SM100_CFG_PAIR_256x256 || cfg == HGEMM_SM100_CFG_PAIR_256x128) ? 256 : 128;
+            const int tn = (cfg == HGEMM_SM100_CFG_PAIR_256x256 || cfg == HGEMM_SM100_CFG_PAIR_128x256) ? 256 : 128;
+            KernelEntry& k = cfg == HGEMM_SM100_CFG_PAIR_256x256   ? g_pair_256
+                             : cfg == HGEMM_SM100_CFG_PAIR_256x128 ? g_pair_128
+                             : cfg == HGEMM_SM100_CFG_PAIR_128x256 ? g_pair_m128_256
+                                                                   : g_pair_m128_128;
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(tm / 2))) != HGEMM_SM100_OK)
+                return rc;
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(k, devid)) != HGEMM_SM100_OK) return rc;
-            const int64_t tiles = cdiv(a.m, 256) * cdiv(a.n, wide ? 256 : 128);
+            const int64_t tiles = cdiv(a.m, tm) * cdiv(a.n, tn);
             const int64_t pairs_max = dev.sms / 2;
             const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
             p.group_m = 8;

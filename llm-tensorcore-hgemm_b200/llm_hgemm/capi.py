@@ -34,6 +34,8 @@ CFG_SPLITK_128x256 = 7
 CFG_STREAMK_128x256 = 8
 CFG_STREAMK_SWAPAB = 9
 CFG_PAIR_256x128 = 10
+CFG_PAIR_128x256 = 11
+CFG_PAIR_128x128 = 12
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2

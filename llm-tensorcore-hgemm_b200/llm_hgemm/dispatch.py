@@ -39,6 +39,8 @@ CUSTOM_PROVIDERS = (
     "tc_streamk_128x256",
     "tc_streamk_swapab",
     "tc_pair_256x128",
+    "tc_pair_128x256",
+    "tc_pair_128x128",
 )
 MISALIGNED_PROVIDER = "auto"
 DEFAULT_PROVIDER = "auto"

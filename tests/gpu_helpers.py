@@ -18,6 +18,8 @@ IMPLEMENTATIONS = [
     "tc_streamk_128x256",
     "tc_streamk_swapab",
     "tc_pair_256x128",
+    "tc_pair_128x256",
+    "tc_pair_128x128",
 ]
 
 

@@ -26,6 +26,8 @@ CONFIG_IDS = {
     "tc_streamk_128x256": capi.CFG_STREAMK_128x256,
     "tc_streamk_swapab": capi.CFG_STREAMK_SWAPAB,
     "tc_pair_256x128": capi.CFG_PAIR_256x128,
+    "tc_pair_128x256": capi.CFG_PAIR_128x256,
+    "tc_pair_128x128": capi.CFG_PAIR_128x128,
 }
 
 

@@ -21,6 +21,8 @@ TMA_CONFIGS = {
     "tc_persistent_128x128": (capi.CFG_PERSISTENT_128x128, (256, 256, 512)),
     "tc_pair_256x256": (capi.CFG_PAIR_256x256, (512, 512, 512)),
     "tc_pair_256x128": (capi.CFG_PAIR_256x128, (512, 512, 512)),
+    "tc_pair_128x256": (capi.CFG_PAIR_128x256, (512, 512, 512)),
+    "tc_pair_128x128": (capi.CFG_PAIR_128x128, (512, 512, 512)),
     "tc_splitk_128x128": (capi.CFG_SPLITK_128x128, (128, 256, 1024)),
     "tc_splitk_128x256": (capi.CFG_SPLITK_128x256, (128, 512, 1024)),
     "tc_swapab": (capi.CFG_SWAPAB, (16, 512, 1024)),
