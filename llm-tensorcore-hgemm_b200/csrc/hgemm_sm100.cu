@@ -224,12 +224,14 @@ struct SwapChoice {
     KernelEntry* k;
     int per_sm;   // CTAs that fit on one SM
 };
-SwapChoice swap_choice(int64_t m) {
-    if (m <= 16) return {16, &g_swap_16, 1};
-    if (m <= 32) return {32, &g_swap_32, 1};
-    if (m <= 64) return {64, &g_swap_64, 1};
-    if (m <= 128) return {128, &g_swap_128, 1};
-    return {256, &g_swap_256, 1};
+SwapChoice swap_of_width(int bnm) {
+    switch (bnm) {
+        case 16: return {16, &g_swap_16, 1};
+        case 32: return {32, &g_swap_32, 1};
+        case 64: return {64, &g_swap_64, 1};
+        case 128: return {128, &g_swap_128, 1};
+        default: return {256, &g_swap_256, 1};
+    }
 }
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
@@ -289,6 +291,108 @@ int fit_split(KernelEntry& k, int dev, int64_t base, int split) {
         --split;
     }
     return split;
+}
+
+// ------------------------------------------------- tile-kernel cost model --
+//
+// Device time (microseconds, constant launch / first-load / store costs
+// left out) of one tile-kernel launch: `tiles` output tiles of `width`
+// accumulator columns, K split `split` ways over `nkb` K blocks, `per_wave`
+// CTAs resident at once, `bytes` of operands read from HBM. Constants were
+// measured on B200 with back-to-back launches on inputs larger than L2:
+// per-K-block time of one CTA by tile width (16: 0.15 us, 32: 0.16, 64: 0.18,
+// 128: 0.22, 256: 0.34 - the MMA issue and TMA feed limits of one SM), HBM
+// at 6.5 TB/s but at most 120 GB/s per streaming CTA, and the split-K
+// exchange (cluster barrier, partial tiles through L2, reduction) at
+// 2 us + 0.05 us per KB of FP32 partial tile.
+double tile_cost(int64_t tiles, int width, int split, int64_t nkb, double bytes, int per_wave) {
+    const double c = width <= 16 ? 0.15 : width <= 32 ? 0.16 : width <= 64 ? 0.18 : width <= 128 ? 0.22 : 0.34;
+    const int64_t wave = per_wave > 0 ? per_wave : 1;
+    const int64_t ctas = tiles * split;
+    const int64_t waves = cdiv(ctas, wave);
+    const double t_main = static_cast<double>(waves) * static_cast<double>(cdiv(nkb, split)) * c;
+    const double streams = static_cast<double>(ctas < wave ? ctas : wave) * 0.12e6;   // bytes per us
+    const double t_mem = bytes / (streams < 6.5e6 ? streams : 6.5e6);
+    const double t_x = split > 1 ? 2.0 + 0.05 * (128.0 * width * 4.0 / 1024.0) : 0.0;
+    return (t_main > t_mem ? t_main : t_mem) + t_x;
+}
+
+// CTAs of kernel `k` resident at once in clusters of `split` (one per SM).
+int wave_ctas(KernelEntry& k, int split, int sms) {
+    int devid = 0;
+    if (split > 1 && cudaGetDevice(&devid) == cudaSuccess) {
+        const int n = max_active_clusters(k, devid, split);
+        if (n > 0) return n * split;
+    }
+    return sms / split * split;
+}
+
+struct TilePlan {
+    int32_t cfg;
+    int width;     // swapped: accumulator columns (output rows) per tile; else 256
+    int32_t split;
+};
+
+// Cheapest tile-kernel plan for (m, n, k): swapped tiles of 16..256 output
+// rows, and (with_wide) 128 x 256 split-K tiles; every K split up to the
+// cluster limit, or only `fixed_split` when given.
+TilePlan plan_tiles_uncached(int64_t m, int64_t n, int64_t k, int sms, int max_split, bool with_swap,
+                             bool with_wide, int32_t fixed_split) {
+    const int64_t nkb = cdiv(k, kBlockK);
+    const double bytes = 2.0 * static_cast<double>(m * k + k * n);
+    TilePlan best{HGEMM_SM100_CFG_SWAPAB, 128, 1};
+    double best_t = -1.0;
+    const int lo = fixed_split > 0 ? fixed_split : 1;
+    const int hi = fixed_split > 0 ? fixed_split : (max_split < nkb ? max_split : static_cast<int>(nkb));
+    auto consider = [&](int32_t cfg, int width, int64_t tiles, KernelEntry& ke) {
+        for (int s = lo; s <= hi; ++s) {
+            // Automatic splits: the cluster sizes the constants were measured with.
+            if (fixed_split <= 0 && s != 1 && s != 2 && s != 3 && s != 4 && s != 6 && s != 8 && s != 16) continue;
+            const double t = tile_cost(tiles, width, s, nkb, bytes, wave_ctas(ke, s, sms));
+            if (best_t < 0.0 || t < best_t) {
+                best_t = t;
+                best = {cfg, width, s};
+            }
+        }
+    };
+    if (with_swap)
+        for (int w : {16, 32, 64, 128, 256}) consider(HGEMM_SM100_CFG_SWAPAB, w, cdiv(n, 128) * cdiv(m, w), *swap_of_width(w).k);
+    if (with_wide) consider(HGEMM_SM100_CFG_SPLITK_128x256, 256, cdiv(m, 128) * cdiv(n, 256), g_splitk_256);
+    return best;
+}
+
+// plan_tiles_uncached, memoised per thread (it is evaluated on every call).
+TilePlan plan_tiles(int64_t m, int64_t n, int64_t k, int sms, int max_split, bool with_swap, bool with_wide,
+                    int32_t fixed_split) {
+    struct Key {
+        int64_t m, n, k;
+        int32_t flags;
+        bool operator==(const Key& o) const { return m == o.m && n == o.n && k == o.k && flags == o.flags; }
+    };
+    struct KeyHash {
+        size_t operator()(const Key& x) const {
+            size_t h = static_cast<size_t>(x.m) * 0x9E3779B97F4A7C15ull;
+            h ^= static_cast<size_t>(x.n) * 0xC2B2AE3D27D4EB4Full + (h << 6) + (h >> 2);
+            h ^= static_cast<size_t>(x.k) * 0x165667B19E3779F9ull + (h << 6) + (h >> 2);
+            return h ^ static_cast<size_t>(x.flags);
+        }
+    };
+    thread_local std::unordered_map<Key, TilePlan, KeyHash> cache;
+    int dev = 0;
+    (void)cudaGetDevice(&dev);
+    const Key key{m, n, k,
+                  (fixed_split << 16) | (dev << 4) | (with_swap ? 1 : 0) | (with_wide ? 2 : 0)};
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    const TilePlan tp = plan_tiles_uncached(m, n, k, sms, max_split, with_swap, with_wide, fixed_split);
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, tp);
+    return tp;
+}
+
+// Swapped-tile width for (m, n, k) at K split `split` (the cheapest).
+SwapChoice swap_choice(int64_t m, int64_t n, int64_t k, int32_t split, int sms, int max_split) {
+    return swap_of_width(plan_tiles(m, n, k, sms, max_split, true, false, split > 0 ? split : 1).width);
 }
 
 int check_args(const HgemmSm100Args* a) {
@@ -355,12 +459,12 @@ bool is_tile_cfg(int32_t cfg) {
            cfg == HGEMM_SM100_CFG_GENERIC_128x128 || cfg == HGEMM_SM100_CFG_SWAPAB;
 }
 
-size_t exchange_bytes(int32_t cfg, int64_t m, int64_t n, int32_t split) {
+size_t exchange_bytes(int32_t cfg, int64_t m, int64_t n, int64_t k, int32_t split, int sms, int max_split) {
     if (!is_tile_cfg(cfg) || split <= 1) return 0;
     int64_t ctas;
     size_t slot;
     if (cfg == HGEMM_SM100_CFG_SWAPAB) {
-        const int bnm = swap_choice(m).bnm;
+        const int bnm = swap_choice(m, n, k, split, sms, max_split).bnm;
         ctas = cdiv(n, 128) * cdiv(m, bnm);
         slot = static_cast<size_t>(128) * bnm * 4;
     } else {
@@ -372,9 +476,9 @@ size_t exchange_bytes(int32_t cfg, int64_t m, int64_t n, int32_t split) {
 }
 
 // Bytes of the kernel's own workspace region (after any staging buffers).
-size_t region_need(int32_t cfg, int32_t split, int64_t m, int64_t n, int64_t k, int sms) {
+size_t region_need(int32_t cfg, int32_t split, int64_t m, int64_t n, int64_t k, int sms, int max_split) {
     if (is_streamk(cfg)) return plan_streamk(cfg, m, n, k, sms).bytes;
-    return exchange_bytes(cfg, m, n, split);
+    return exchange_bytes(cfg, m, n, k, split, sms, max_split);
 }
 
 std::atomic<uint64_t> g_epoch_counter{0};
@@ -456,9 +560,15 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
     } else if (cfg == HGEMM_SM100_CFG_AUTO) {
         // At least one tile per SM: persistent waves (+ a stream-K split tail).
         // Fewer tiles than SMs: one tile per CTA, K split across a cluster.
-        if (a.m <= 128) {
-            const int64_t tiles = cdiv(a.n, 128);
-            cfg = tiles >= sms ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_SWAPAB;
+        const int64_t wide_tiles = cdiv(a.m, 128) * cdiv(a.n, 256);
+        if (a.m <= 128 && cdiv(a.n, 128) >= sms) {
+            cfg = HGEMM_SM100_CFG_STREAMK_SWAPAB;
+        } else if (a.m <= 512 && wide_tiles < sms) {
+            // Few tiles: the cost model picks the tile width and K split.
+            const TilePlan tp = plan_tiles(a.m, a.n, a.k, sms, dev.max_cluster, true, a.m > 128, a.split_k);
+            *cfg_out = tp.cfg;
+            *split_out = tp.split;
+            return HGEMM_SM100_OK;
         } else {
             // >= 4 waves: the partial last wave costs little, the plain
             // persistent kernel runs the waves fastest.
@@ -476,7 +586,6 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             }
         }
     }
-    if (cfg == HGEMM_SM100_CFG_SWAPAB && a.m > 256) cfg = HGEMM_SM100_CFG_SPLITK_128x256;
     if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB && a.m > 128) cfg = HGEMM_SM100_CFG_STREAMK_128x256;
     if (is_streamk(cfg) && !assume_workspace) {
         const StreamKPlan sp = plan_streamk(cfg, a.m, a.n, a.k, sms);
@@ -492,8 +601,15 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
         cfg == HGEMM_SM100_CFG_GENERIC_128x128 || cfg == HGEMM_SM100_CFG_SWAPAB) {
         int64_t base;
         int per_sm = 1;
+        if (cfg == HGEMM_SM100_CFG_SWAPAB && a.split_k <= 0) {
+            // Width and split from the cost model (the split already fits
+            // the clusters that can be resident).
+            *cfg_out = cfg;
+            *split_out = plan_tiles(a.m, a.n, a.k, sms, dev.max_cluster, true, false, 0).split;
+            return HGEMM_SM100_OK;
+        }
         if (cfg == HGEMM_SM100_CFG_SWAPAB) {
-            const SwapChoice sc = swap_choice(a.m);
+            const SwapChoice sc = swap_choice(a.m, a.n, a.k, a.split_k, sms, dev.max_cluster);
             base = cdiv(a.n, 128) * cdiv(a.m, sc.bnm);
             per_sm = sc.per_sm;
         } else if (cfg == HGEMM_SM100_CFG_SPLITK_128x256) {
@@ -505,7 +621,7 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
         if (split > nkb) split = static_cast<int32_t>(nkb);
         if (split < 1) split = 1;
         if (a.split_k <= 0 && split > 1) {
-            KernelEntry* k = cfg == HGEMM_SM100_CFG_SWAPAB          ? swap_choice(a.m).k
+            KernelEntry* k = cfg == HGEMM_SM100_CFG_SWAPAB ? swap_choice(a.m, a.n, a.k, split, sms, dev.max_cluster).k
                              : cfg == HGEMM_SM100_CFG_SPLITK_128x256 ? &g_splitk_256
                              : cfg == HGEMM_SM100_CFG_SPLITK_128x128 ? &g_splitk_128
                                                                      : &g_generic_128;
@@ -607,7 +723,8 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
         return r;
     };
     // Split-K partial exchange through the workspace when the caller gave one.
-    if (split > 1 && region != nullptr && region_bytes >= exchange_bytes(cfg, a.m, a.n, split))
+    if (split > 1 && region != nullptr &&
+        region_bytes >= exchange_bytes(cfg, a.m, a.n, a.k, split, dev.sms, dev.max_cluster))
         p.partials = reinterpret_cast<float*>(region);
     const uint64_t M = a.m, N = a.n, K = a.k;
 
@@ -660,7 +777,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             return launch(k, grid, split, map_k, map_mn, map_c, p, stream);
         }
         case HGEMM_SM100_CFG_SWAPAB: {
-            const SwapChoice sc = swap_choice(a.m);
+            const SwapChoice sc = swap_choice(a.m, a.n, a.k, split, dev.sms, dev.max_cluster);
             if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, static_cast<uint32_t>(sc.bnm))) !=
                 HGEMM_SM100_OK)
                 return rc;
@@ -745,7 +862,7 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     size_t region_bytes = 0;
     const size_t region_off = align_up(staged ? st.total : 0, kStageAlign);
     if (ws != nullptr && reinterpret_cast<uintptr_t>(ws) % kStageAlign == 0 && args->workspace_bytes > region_off &&
-        region_need(cfg, split, args->m, args->n, args->k, dev->sms) > 0) {
+        region_need(cfg, split, args->m, args->n, args->k, dev->sms, dev->max_cluster) > 0) {
         region = ws + region_off;
         region_bytes = static_cast<size_t>(args->workspace_bytes) - region_off;
     }
@@ -792,7 +909,7 @@ extern "C" size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args) {
     int32_t cfg = 0, split = 0;
     resolve_cfg(*args, *dev, true, &cfg, &split);
     if (cfg == HGEMM_SM100_CFG_GENERIC_128x128) return 0;
-    const size_t region = region_need(cfg, split, args->m, args->n, args->k, dev->sms);
+    const size_t region = region_need(cfg, split, args->m, args->n, args->k, dev->sms, dev->max_cluster);
     if (region > 0) total = align_up(total, kStageAlign) + region;
     return total;
 }
@@ -830,7 +947,7 @@ extern "C" size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t
     a.config = config;
     int32_t cfg = 0, split = 0;
     if (resolve_cfg(a, *dev, true, &cfg, &split) != HGEMM_SM100_OK) return 0;
-    return exchange_bytes(cfg, m, n, split);
+    return exchange_bytes(cfg, m, n, k, split, dev->sms, dev->max_cluster);
 }
 
 extern "C" const char* hgemm_sm100_status_string(int status) {
