@@ -122,19 +122,21 @@ int32_t hgemm_sm100_config_from_name(const char* name);
 const char* hgemm_sm100_config_name(int32_t config);
 int32_t hgemm_sm100_num_configs(void);
 
-/* Global-memory workspace a configuration needs independent of the operands'
- * alignment: 0 for the split-K configurations (partials are reduced through
- * distributed shared memory); for the stream-K configurations the per-CTA
- * slots for an (m, n, k) problem on the current device. Counterpart of
+/* Global-memory workspace a configuration uses for an (m, n, k) problem with
+ * aligned operands on the current device: the stream-K configurations' per-CTA
+ * slots and flags, or the split-K tile configurations' partial-tile exchange
+ * (at the split the library chooses); 0 otherwise. Counterpart of
  * backend_info()["workspace_bytes"] (reference csrc/dispatch.cpp:104-128). */
 size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k);
 
 /* Workspace bytes hgemm_sm100_run needs for `args`: staging buffers for
  * operands that TMA cannot describe, plus, when the call resolves to a
- * stream-K configuration, one FP32 partial-tile slot and one flag per CTA.
- * 0 when neither applies. Queries the current device's SM count (cached);
- * launches nothing. The stream-K part keeps no state between calls: any
- * workspace of this size works, whatever it contains. */
+ * stream-K configuration, one FP32 partial-tile slot and one flag per CTA,
+ * or, for a split-K tile configuration, one FP32 partial tile per CTA
+ * (exchanged through L2; without it the partials go through distributed
+ * shared memory). 0 when none applies. Queries the current device (cached);
+ * launches nothing. No state is kept between calls: any workspace of this
+ * size works, whatever it contains. */
 size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
 
 /* Runs C = A @ B like hgemm_sm100_run, but takes no workspace and allocates

@@ -476,6 +476,11 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // The set-up above touches only this CTA's shared memory and TMEM, so it
+    // may overlap the previous kernel of the stream; global memory is only
+    // touched after that kernel has completed.
+    grid_dependents_launch();
+    grid_dependency_wait();
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     const int acc_row0 = blockIdx.x * kMmaM;   // accumulator rows (M, or N when swapped)
@@ -823,6 +828,11 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // The set-up above touches only this CTA's shared memory and TMEM, so it
+    // may overlap the previous kernel of the stream; global memory is only
+    // touched after that kernel has completed.
+    grid_dependents_launch();
+    grid_dependency_wait();
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     const int tiles_m = (p.m + kMmaM - 1) / kMmaM;
@@ -1014,6 +1024,11 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     cluster_sync();                       // both CTAs' barriers exist before any remote op
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // The set-up above touches only this CTA's shared memory and TMEM, so it
+    // may overlap the previous kernel of the stream; global memory is only
+    // touched after that kernel has completed.
+    grid_dependents_launch();
+    grid_dependency_wait();
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     const int tiles_m = (p.m + Cfg::kTileM - 1) / Cfg::kTileM;
@@ -1290,6 +1305,11 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     __syncthreads();
     tc_fence_after_sync();
     const uint32_t tmem_base = *tmem_slot;
+    // The set-up above touches only this CTA's shared memory and TMEM, so it
+    // may overlap the previous kernel of the stream; global memory is only
+    // touched after that kernel has completed.
+    grid_dependents_launch();
+    grid_dependency_wait();
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     // Accumulator tiles: rows = M (N when swapped) in 128s, cols = kBNm wide.

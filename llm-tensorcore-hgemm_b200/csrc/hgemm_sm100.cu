@@ -563,7 +563,7 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
         const int64_t wide_tiles = cdiv(a.m, 128) * cdiv(a.n, 256);
         if (a.m <= 128 && cdiv(a.n, 128) >= sms) {
             cfg = HGEMM_SM100_CFG_STREAMK_SWAPAB;
-        } else if (a.m <= 512 && wide_tiles < sms) {
+        } else if (a.m <= 2048 && wide_tiles < sms) {
             // Few tiles: the cost model picks the tile width and K split.
             const TilePlan tp = plan_tiles(a.m, a.n, a.k, sms, dev.max_cluster, true, a.m > 128, a.split_k);
             *cfg_out = tp.cfg;
@@ -646,7 +646,7 @@ int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = k.smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[3];
     unsigned n = 0;
     if (cluster_z > 1 || cluster_x > 1) {
         attr[n].id = cudaLaunchAttributeClusterDimension;
@@ -659,6 +659,13 @@ int launch(const KernelEntry& k, dim3 grid, int cluster_z, const CUtensorMap& m0
         // Stream-K finishers wait for other CTAs: all must be resident.
         attr[n].id = cudaLaunchAttributeCooperative;
         attr[n].val.cooperative = 1;
+        ++n;
+    } else {
+        // Programmatic dependent launch: the kernel's set-up overlaps the
+        // previous kernel of the stream (the kernels wait for it before
+        // touching global memory).
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
         ++n;
     }
     if (n > 0) {

@@ -210,6 +210,17 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                  : "memory");
 }
 
+// Programmatic dependent launch. launch_dependents lets the next grid of
+// the stream be scheduled before this one ends; wait blocks until the grids
+// this one depends on have completed and their memory is visible (a no-op
+// for a launch without that dependency).
+__device__ __forceinline__ void grid_dependents_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Barrier among the 128 threads of warps 0-3 (named barrier 1).
 __device__ __forceinline__ void epilogue_bar_sync() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
