@@ -1454,30 +1454,37 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                     uint32_t v0[32], v1[32];
                     tmem_ld_32x32b_x32(t_acc + c, v0);
                     tmem_ld_32x32b_x32(t_acc + c + 32, v1);
-                    tmem_wait_ld();
                     if (finish) {
+                        // The 16 partial quads of this row's 64 columns, loaded
+                        // together (overlapping the TMEM loads), then added.
+                        float4 part[16];
+                        const size_t q0 = static_cast<size_t>(c / 4) * kMmaM + r;
+                        if (one_producer) {
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            uint32_t* v = h ? v1 : v0;
+                            for (int q = 0; q < 16; ++q) part[q] = staged[q0 + static_cast<size_t>(q) * kMmaM];
+                        } else {
 #pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                const size_t qi = static_cast<size_t>((c + 32 * h + j) / 4) * kMmaM + r;
-                                float4 sum;
-                                if (one_producer) {
-                                    sum = staged[qi];
-                                } else {
-                                    sum = __ldcg(slots + static_cast<size_t>(p_lo) * kSlotQuads + qi);
-                                    for (int q = p_lo + 1; q < g; ++q) {
-                                        const float4 x = __ldcg(slots + static_cast<size_t>(q) * kSlotQuads + qi);
-                                        sum.x += x.x; sum.y += x.y; sum.z += x.z; sum.w += x.w;
-                                    }
+                            for (int q = 0; q < 16; ++q)
+                                part[q] = __ldcg(slots + static_cast<size_t>(p_lo) * kSlotQuads + q0 + static_cast<size_t>(q) * kMmaM);
+                            for (int s2 = p_lo + 1; s2 < g; ++s2) {
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) {
+                                    const float4 x = __ldcg(slots + static_cast<size_t>(s2) * kSlotQuads + q0 + static_cast<size_t>(q) * kMmaM);
+                                    part[q].x += x.x; part[q].y += x.y; part[q].z += x.z; part[q].w += x.w;
                                 }
-                                v[j] = __float_as_uint(sum.x + __uint_as_float(v[j]));
-                                v[j + 1] = __float_as_uint(sum.y + __uint_as_float(v[j + 1]));
-                                v[j + 2] = __float_as_uint(sum.z + __uint_as_float(v[j + 2]));
-                                v[j + 3] = __float_as_uint(sum.w + __uint_as_float(v[j + 3]));
                             }
                         }
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            uint32_t* v = q < 8 ? v0 + 4 * q : v1 + 4 * (q - 8);
+                            v[0] = __float_as_uint(part[q].x + __uint_as_float(v[0]));
+                            v[1] = __float_as_uint(part[q].y + __uint_as_float(v[1]));
+                            v[2] = __float_as_uint(part[q].z + __uint_as_float(v[2]));
+                            v[3] = __float_as_uint(part[q].w + __uint_as_float(v[3]));
+                        }
+                    } else {
+                        tmem_wait_ld();
                     }
                     store_box_tma(&tm_c, boxes + epi_buf * 4096u, lane, v0, v1, tc * kBNm + c,
                                   tr * kMmaM + warp * 32);
