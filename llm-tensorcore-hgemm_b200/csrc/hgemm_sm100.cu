@@ -570,15 +570,20 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             *split_out = tp.split;
             return HGEMM_SM100_OK;
         } else {
-            // >= 4 waves: the plain persistent kernel runs the waves fastest
-            // and a partial last wave costs little - unless it is less than
-            // half full within the first 8 waves (stream-K then spreads it).
+            // At least one wave: the persistent kernel runs whole tiles; its
+            // partial last wave leaves SMs idle for (1 - fill) of a wave.
+            // Stream-K spreads that tail but pays its partial-tile fixup
+            // (about 6 us). It is used below 8 waves when the idle time it
+            // removes (a 128 x 256 tile's K block takes about 0.30 us) is
+            // larger than that.
             const int64_t tiles = cdiv(a.m, 128) * cdiv(a.n, 256);
             const int64_t waves = tiles / sms, rem = tiles % sms;
-            const bool thin_tail = waves < 8 && rem > 0 && 2 * rem < sms;
-            cfg = (tiles >= 4 * static_cast<int64_t>(sms) && !thin_tail) ? HGEMM_SM100_CFG_PERSISTENT_128x256
-                  : tiles >= sms                                       ? HGEMM_SM100_CFG_STREAMK_128x256
-                                                                       : HGEMM_SM100_CFG_SPLITK_128x256;
+            const double idle_us = rem == 0 ? 0.0
+                                            : (1.0 - static_cast<double>(rem) / sms) * 0.30 * static_cast<double>(nkb);
+            const bool spread_tail = waves < 8 && idle_us > 6.0;
+            cfg = tiles < sms      ? HGEMM_SM100_CFG_SPLITK_128x256
+                  : spread_tail    ? HGEMM_SM100_CFG_STREAMK_128x256
+                                   : HGEMM_SM100_CFG_PERSISTENT_128x256;
             // Narrow tiles when they (with their K split) fill the SMs in one
             // wave: the same MMA time per K block, half the partial tile to
             // exchange, or no split at all.
