@@ -303,8 +303,9 @@ int fit_split(KernelEntry& k, int dev, int64_t base, int split) {
 // per-K-block time of one CTA by tile width (16: 0.15 us, 32: 0.16, 64: 0.18,
 // 128: 0.22, 256: 0.34 - the MMA issue and TMA feed limits of one SM), HBM
 // at 6.5 TB/s but at most 120 GB/s per streaming CTA, and the split-K
-// exchange (cluster barrier, partial tiles through L2, reduction) at
-// 2 us + 0.05 us per KB of FP32 partial tile.
+// exchange (cluster barrier and reduction; partial tiles through distributed
+// shared memory up to 128 columns, through L2 above) at 1.2 us + 0.04 us per
+// KB of FP32 partial tile, respectively 2 us + 0.05 us per KB.
 double tile_cost(int64_t tiles, int width, int split, int64_t nkb, double bytes, int per_wave) {
     const double c = width <= 16 ? 0.15 : width <= 32 ? 0.16 : width <= 64 ? 0.18 : width <= 128 ? 0.22 : 0.34;
     const int64_t wave = per_wave > 0 ? per_wave : 1;
@@ -313,7 +314,8 @@ double tile_cost(int64_t tiles, int width, int split, int64_t nkb, double bytes,
     const double t_main = static_cast<double>(waves) * static_cast<double>(cdiv(nkb, split)) * c;
     const double streams = static_cast<double>(ctas < wave ? ctas : wave) * 0.12e6;   // bytes per us
     const double t_mem = bytes / (streams < 6.5e6 ? streams : 6.5e6);
-    const double t_x = split > 1 ? 2.0 + 0.05 * (128.0 * width * 4.0 / 1024.0) : 0.0;
+    const double kb_partial = 128.0 * width * 4.0 / 1024.0;
+    const double t_x = split <= 1 ? 0.0 : width <= 128 ? 1.2 + 0.04 * kb_partial : 2.0 + 0.05 * kb_partial;
     return (t_main > t_mem ? t_main : t_mem) + t_x;
 }
 
@@ -346,9 +348,12 @@ TilePlan plan_tiles_uncached(int64_t m, int64_t n, int64_t k, int sms, int max_s
     const int hi = fixed_split > 0 ? fixed_split : (max_split < nkb ? max_split : static_cast<int>(nkb));
     auto consider = [&](int32_t cfg, int width, int64_t tiles, KernelEntry& ke) {
         for (int s = lo; s <= hi; ++s) {
-            // Automatic splits: the cluster sizes the constants were measured with.
+            // Automatic splits: the cluster sizes the constants were measured
+            // with, in one wave (waves of clusters cost far more than modelled).
             if (fixed_split <= 0 && s != 1 && s != 2 && s != 3 && s != 4 && s != 6 && s != 8 && s != 16) continue;
-            const double t = tile_cost(tiles, width, s, nkb, bytes, wave_ctas(ke, s, sms));
+            const int wave = wave_ctas(ke, s, sms);
+            if (fixed_split <= 0 && s > 1 && tiles * s > wave) continue;
+            const double t = tile_cost(tiles, width, s, nkb, bytes, wave);
             if (best_t < 0.0 || t < best_t) {
                 best_t = t;
                 best = {cfg, width, s};
@@ -453,7 +458,10 @@ StreamKPlan plan_streamk(int32_t cfg, int64_t m, int64_t n, int64_t k, int sms) 
 
 // Split-K tile kernels: workspace for exchanging FP32 partial tiles, one slot
 // per CTA (0 when there is no split). Without it the partials go through
-// distributed shared memory.
+// distributed shared memory, which is also the faster transport for tiles of
+// at most 128 columns (partials up to 64 KB per CTA: remote stores plus one
+// cluster barrier beat the two L2 round trips); the workspace serves the
+// 256-column tiles (128 KB partials).
 bool is_tile_cfg(int32_t cfg) {
     return cfg == HGEMM_SM100_CFG_SPLITK_128x128 || cfg == HGEMM_SM100_CFG_SPLITK_128x256 ||
            cfg == HGEMM_SM100_CFG_GENERIC_128x128 || cfg == HGEMM_SM100_CFG_SWAPAB;
@@ -465,10 +473,12 @@ size_t exchange_bytes(int32_t cfg, int64_t m, int64_t n, int64_t k, int32_t spli
     size_t slot;
     if (cfg == HGEMM_SM100_CFG_SWAPAB) {
         const int bnm = swap_choice(m, n, k, split, sms, max_split).bnm;
+        if (bnm <= 128) return 0;
         ctas = cdiv(n, 128) * cdiv(m, bnm);
         slot = static_cast<size_t>(128) * bnm * 4;
     } else {
         const int bn = cfg == HGEMM_SM100_CFG_SPLITK_128x256 ? 256 : 128;
+        if (bn <= 128) return 0;
         ctas = cdiv(m, 128) * cdiv(n, bn);
         slot = static_cast<size_t>(128) * (bn + 4) * 4;
     }
