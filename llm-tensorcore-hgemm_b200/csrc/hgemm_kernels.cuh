@@ -1241,7 +1241,9 @@ struct StreamKCfg {
     static constexpr uint32_t kKBytes = kKRows * 128u;
     static constexpr uint32_t kMNBytes = kMNCols * 128u;
     static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
-    static constexpr uint32_t kEpiBytes = kSwap ? 0u : 4u * 2u * 4096u;   // TMA-store boxes
+    // TMA-store boxes, two per epilogue warp: 32 x 64 halves, or (swapped)
+    // kChunk x 32 halves.
+    static constexpr uint32_t kEpiBytes = kSwap ? 4u * 2u * 2048u : 4u * 2u * 4096u;
     static constexpr uint32_t kDataBytes = kStages * kStageBytes + kEpiBytes;
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
@@ -1529,7 +1531,13 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                         }
                     }
                     if constexpr (kSwap) {
-                        store_col_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
+                        if (p.tma_store) {
+                            store_box_tma_t<Cfg::kChunk>(&tm_c, smem + kStages * Cfg::kStageBytes + warp * 4096u + epi_buf * 2048u,
+                                                         lane, v, tr * kMmaM + static_cast<int>(warp) * 32, tc * kBNm + c);
+                            epi_buf ^= 1u;
+                        } else {
+                            store_col_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
+                        }
                     } else {
                         store_row_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
                     }
@@ -1553,7 +1561,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                     for (int q = p_lo; q < g; ++q) p.flags[q] = 0ull;
             }
         }
-        if (!kSwap && p.tma_store && lane == 0) bulk_wait_group_all();
+        if (p.tma_store && lane == 0) bulk_wait_group_all();
     }
 
     __syncwarp();

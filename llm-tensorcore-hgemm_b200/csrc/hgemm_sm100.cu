@@ -824,7 +824,8 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
                 return rc;
             }
             if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
-            if (!sp.swap && (rc = prepare_store()) != HGEMM_SM100_OK) return rc;
+            if ((rc = sp.swap ? prepare_store(32, sp.bnm >= 32 ? 32 : 16, false) : prepare_store()) != HGEMM_SM100_OK)
+                return rc;
             if ((rc = prepare_kernel(*sp.k, devid)) != HGEMM_SM100_OK) return rc;
             p.streamk = sp.streamk;
             p.group_m = sp.swap ? 1 : 16;
