@@ -306,8 +306,20 @@ template <int kBNm, bool kSwap, bool kTma, int kStages>
 struct TileCfg {
     static constexpr int kKRows = kSwap ? kBNm : kMmaM;     // rows of the K-major tile
     static constexpr int kMNCols = kSwap ? kMmaM : kBNm;    // cols of the MN-major tile
-    static constexpr uint32_t kKBytes = kKRows * 128u;
-    static constexpr uint32_t kMNBytes = kMNCols * 128u;
+    // Two TMA producers and two MMA issuers with an accumulator each for
+    // tiles of at most 128 columns fed by TMA (see the kernel); one of each
+    // otherwise. Each producer owns the stages of one parity.
+    static constexpr bool kDual = kTma && kBNm <= 128;
+    // K per stage. A stage holds kKB / 64 K-major atoms of kKRows x 64
+    // halves, and per 64-column MN-major chunk kKB rows. (128-deep stages -
+    // 8 MMAs per barrier hand-off - measured no faster than 64-deep ones
+    // with twice the ring depth once the tile runs two producers and two
+    // issuers.)
+    static constexpr int kKB = 64;
+    static constexpr uint32_t kKAtomBytes = kKRows * 128u;
+    static constexpr uint32_t kMNChunkBytes = kKB * 128u;
+    static constexpr uint32_t kKBytes = kKAtomBytes * (kKB / 64);
+    static constexpr uint32_t kMNBytes = (kMNCols / 64) * kMNChunkBytes;
     static constexpr uint32_t kStageBytes = kKBytes + kMNBytes;
     // Split-K receive buffer (FP32): accumulator rows are divided among the
     // CTAs of the cluster in whole quads of 4 rows (rank r owns rows from
@@ -316,22 +328,16 @@ struct TileCfg {
     // output's contiguous dimension contiguous, quads 16-byte aligned). Rows
     // per rank <= 4 * ceil(32 / split); over split 2..16,
     // split * 4 * ceil(32 / split) <= 180. The buffer reuses the stage ring
-    // once every CTA's MMAs are done (the ring is deep for narrow tiles).
-    static constexpr bool kRecvOwn = false;
+    // once every CTA's MMAs are done.
     static constexpr uint32_t kRecvBytes = kSwap ? 180u * kBNm * 4u : 180u * (kBNm + 4) * 4u;
-    static constexpr uint32_t kRecvOff = kRecvOwn ? kStages * kStageBytes : 0u;
+    static constexpr uint32_t kRecvOff = 0u;
     // Workspace exchange: one FP32 tile per CTA, staged in the stage ring.
     static constexpr uint32_t kSlotFloats = kSwap ? 128u * kBNm : 128u * (kBNm + 4);
     static_assert(kSlotFloats * 4u <= kStages * kStageBytes, "staging fits the stage ring");
     static_assert(kSwap || kStages * kStageBytes >= 4u * 8192u, "TMA-store boxes fit the stage ring");
-    static constexpr uint32_t kDataBytes =
-        kRecvOwn ? kStages * kStageBytes + kRecvBytes : cmax(kStages * kStageBytes, kRecvBytes);
+    static constexpr uint32_t kDataBytes = cmax(kStages * kStageBytes, kRecvBytes);
     static constexpr uint32_t kBarBytes = 256;
     static constexpr uint32_t kSmemBytes = kDataBytes + kBarBytes + 1024;
-    // Two TMA producers and two MMA issuers with an accumulator each for
-    // tiles of at most 128 columns fed by TMA (see the kernel); one of each
-    // otherwise. Each producer owns the stages of one parity.
-    static constexpr bool kDual = kTma && kBNm <= 128;
     static_assert(!kDual || kStages % 2 == 0, "dual producers own alternate stages");
     static constexpr uint32_t kTmemCols = tmem_cols_for(kDual ? 2 * kBNm : kBNm);
     static constexpr uint32_t kIdesc = make_idesc_f16(kMmaM, kBNm, kSwap, !kSwap);
@@ -487,7 +493,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     const int acc_col0 = blockIdx.y * kBNm;    // accumulator cols (N, or M when swapped)
     const int k_rows0 = kSwap ? acc_col0 : acc_row0;   // first A row of the K-major tile
     const int mn_cols0 = kSwap ? acc_row0 : acc_col0;  // first B column of the MN-major tile
-    const int nkb = (p.k + kBlockK - 1) / kBlockK;
+    const int nkb = (p.k + Cfg::kKB - 1) / Cfg::kKB;   // K blocks of this kernel
     const int split = gridDim.z;
     const int kb0 = static_cast<int>(blockIdx.z) * nkb / split;
     const int kb1 = (static_cast<int>(blockIdx.z) + 1) * nkb / split;
@@ -512,11 +518,15 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
                 uint8_t* s_mn = s_k + Cfg::kKBytes;
                 const uint32_t extra = (p.inject && kb == kb0) ? 16u : 0u;
                 mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes + extra);
-                tma_load_2d(s_k, &tm_k, &full[stage], kb * kBlockK, k_rows0);
 #pragma unroll
-                for (int j = 0; j < Cfg::kMNCols / 64; ++j)
-                    tma_load_2d(s_mn + j * kChunkBytes, &tm_mn, &full[stage], mn_cols0 + 64 * j,
-                                kb * kBlockK);
+                for (int h = 0; h < Cfg::kKB / 64; ++h) {
+                    const int k0 = kb * Cfg::kKB + 64 * h;
+                    tma_load_2d(s_k + h * Cfg::kKAtomBytes, &tm_k, &full[stage], k0, k_rows0);
+#pragma unroll
+                    for (int j = 0; j < Cfg::kMNCols / 64; ++j)
+                        tma_load_2d(s_mn + j * Cfg::kMNChunkBytes + h * kChunkBytes, &tm_mn, &full[stage],
+                                    mn_cols0 + 64 * j, k0);
+                }
                 ++issued;
             }
             if (!ok || *abort_flag) drain_tma<kStages, kStep>(full, issued, static_cast<uint32_t>(which));
@@ -558,9 +568,9 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
             const uint32_t s_k = smem_addr(smem + stage * Cfg::kStageBytes);
             const uint32_t s_mn = s_k + Cfg::kKBytes;
 #pragma unroll
-            for (int kk = 0; kk < kBlockK / 16; ++kk) {
-                const uint64_t dk = kmaj_desc(s_k, kk);
-                const uint64_t dmn = mnmaj_desc(s_mn, kk);
+            for (int kk = 0; kk < Cfg::kKB / 16; ++kk) {
+                const uint64_t dk = make_smem_desc(s_k + (kk >> 2) * Cfg::kKAtomBytes + (kk & 3) * 32u, 16u, 1024u);
+                const uint64_t dmn = make_smem_desc(s_mn + kk * 2048u, Cfg::kMNChunkBytes, 1024u);
                 tc_mma_f16(d, kSwap ? dmn : dk, kSwap ? dk : dmn, Cfg::kIdesc, (!first || kk > 0) ? 1u : 0u);
             }
             first = false;
@@ -610,7 +620,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
     }
     // Push receive buffers inside the stage ring: every CTA's MMAs must be
     // done (its tfull observed above) before anyone writes into it.
-    if (split_k && !via_l2 && !Cfg::kRecvOwn) cluster_sync();
+    if (split_k && !via_l2) cluster_sync();
     if (warp < 4) {
         if (ok) {
             const int r = warp * 32 + lane;   // accumulator row = TMEM lane

@@ -335,6 +335,14 @@ struct TilePlan {
     int32_t split;
 };
 
+// K blocks of a tile configuration (TileCfg::kKB = 64 for every width); a
+// K split never exceeds their number.
+int64_t tile_kblocks(int32_t cfg, int width, int64_t k) {
+    (void)cfg;
+    (void)width;
+    return cdiv(k, kBlockK);
+}
+
 // Cheapest tile-kernel plan for (m, n, k): swapped tiles of 16..256 output
 // rows, and (with_wide) 128 x 256 split-K tiles; every K split up to the
 // cluster limit, or only `fixed_split` when given.
@@ -344,9 +352,11 @@ TilePlan plan_tiles_uncached(int64_t m, int64_t n, int64_t k, int sms, int max_s
     const double bytes = 2.0 * static_cast<double>(m * k + k * n);
     TilePlan best{HGEMM_SM100_CFG_SWAPAB, 128, 1};
     double best_t = -1.0;
-    const int lo = fixed_split > 0 ? fixed_split : 1;
-    const int hi = fixed_split > 0 ? fixed_split : (max_split < nkb ? max_split : static_cast<int>(nkb));
     auto consider = [&](int32_t cfg, int width, int64_t tiles, KernelEntry& ke) {
+        const int64_t blocks = tile_kblocks(cfg, width, k);
+        if (fixed_split > blocks) return;   // a given split needs that many K blocks
+        const int lo = fixed_split > 0 ? fixed_split : 1;
+        const int hi = fixed_split > 0 ? fixed_split : (max_split < blocks ? max_split : static_cast<int>(blocks));
         for (int s = lo; s <= hi; ++s) {
             // Automatic splits: the cluster sizes the constants were measured
             // with, in one wave (waves of clusters cost far more than modelled).
