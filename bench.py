@@ -468,8 +468,29 @@ def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict
     h2d_rank = (x_h.numel() + h_h.numel()) * 2
     d2h_rank = out_h.numel() * 2
     del x_h, h_h, out_h
+
+    # Down-projection variants (max over ranks): the FP32 all-reduce of the
+    # headline, and reduce-scatter to an FP16 row shard, without and with
+    # chunked comm/compute overlap.
+    def timed_max(fn, steps):
+        tm = torch.tensor([device_time_ms(fn, steps, 2, stream, barrier) / steps], device=dev,
+                          dtype=torch.float64)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        return float(tm.item())
+
+    vsteps = max(3, min(args.steps, 10))
+    variants = {"all_reduce_ms": timed_max(mlp.down, vsteps),
+                "reduce_scatter_ms": timed_max(lambda: mlp.down_scatter(1), vsteps)}
+    chunks = 4 if mlp.x.shape[0] % (4 * world) == 0 else 1
+    variants[f"reduce_scatter_overlap{chunks}_ms"] = timed_max(lambda: mlp.down_scatter(chunks), vsteps)
+    mlp.down()
+    shard = mlp.down_scatter(chunks)
+    rows = mlp.owned_rows(chunks).to(dev)
+    d = shard.float() - mlp.out[rows].float()
+    rel = torch.linalg.vector_norm(d) / torch.linalg.vector_norm(mlp.out[rows].float()).clamp_min(1e-12)
+    scatter_ok = bool(torch.isfinite(shard.float()).all()) and d.abs().max().item() <= 5e-2 and rel.item() <= 5e-3
     ok = mlp.check()
-    okt = torch.tensor([1 if ok else 0], device=dev)
+    okt = torch.tensor([1 if (ok and scatter_ok) else 0], device=dev)
     dist.all_reduce(okt, op=dist.ReduceOp.MIN)
     if rank != 0:
         return None
@@ -500,6 +521,7 @@ def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict
         "correctness": "pass" if int(okt.item()) else "fail",
         "breakdown_ms": {"gemms": round(gemm_ms, 4), "step": round(ms_max, 4),
                          "all_reduce_and_rounding": round(max(0.0, ms_max - gemm_ms), 4)},
+        "down_proj_variants_ms": {k: round(v, 4) for k, v in variants.items()},
     }
 
 

@@ -81,12 +81,30 @@ enum {
                                               pipeline wait runs out */
 };
 
+/* Fused epilogue (HgemmSm100Args.epilogue, a bit set; 0 = C = A @ B). Every
+ * term is added to the FP32 accumulator and the result rounded to FP16 once,
+ * by the CTA that stores the final sum (split-K and stream-K partials stay
+ * raw). Not combinable with HGEMM_SM100_FLAG_OUT_F32. The reference accepts
+ * only epilogue "none" (csrc/dispatch.cpp:52); these extend that argument. */
+enum {
+    HGEMM_SM100_EPI_BIAS = 1,      /* + bias[j], FP16 [n]                         */
+    HGEMM_SM100_EPI_RESIDUAL = 2,  /* + residual[i, j], FP16 [m x ldr] (ldr >= n); it
+                                      may be C itself (ldr == ldc): each element
+                                      is read before it is written              */
+    HGEMM_SM100_EPI_SILU_MUL = 4   /* SwiGLU: B's columns hold (gate, up) pairs
+                                      2j, 2j + 1 and C[i, j] = silu(g) * u with
+                                      g, u the FP32 sums of those columns (after
+                                      the bias); n even, C is [m x n/2]
+                                      (ldc >= n/2); not with EPI_RESIDUAL       */
+};
+
 typedef struct HgemmSm100Args {
     const void* a;       /* FP16 [m x lda], row-major, device memory          */
     const void* b;       /* FP16 [k x ldb], row-major                         */
     void* c;             /* FP16 (or FP32 with FLAG_OUT_F32) [m x ldc]        */
     int64_t m, n, k;     /* > 0, each < 2^31                                   */
-    int64_t lda, ldb, ldc;  /* leading dimensions in elements (>= k, n, n)    */
+    int64_t lda, ldb, ldc;  /* leading dimensions in elements (>= k, n, n;
+                               ldc >= n/2 with EPI_SILU_MUL)                 */
     int32_t config;      /* HGEMM_SM100_CFG_*                                 */
     int32_t split_k;     /* 0 = choose; else K splits (1..16), split configs  */
     int32_t flags;       /* HGEMM_SM100_FLAG_*                                */
@@ -97,6 +115,11 @@ typedef struct HgemmSm100Args {
                             TMA cannot describe (see hgemm_sm100_workspace_size);
                             NULL = no staging                                 */
     uint64_t workspace_bytes;
+    int32_t epilogue;    /* HGEMM_SM100_EPI_* bits; 0 = plain C = A @ B       */
+    int32_t reserved;    /* 0                                                 */
+    const void* bias;    /* FP16 [n], device memory, with EPI_BIAS            */
+    const void* residual;/* FP16 [m x ldr], device memory, with EPI_RESIDUAL  */
+    int64_t ldr;         /* residual leading dimension in elements            */
 } HgemmSm100Args;
 
 /* Launches C = A @ B on `stream` (a cudaStream_t; NULL = legacy default) on
@@ -167,6 +190,56 @@ size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
  *   on two streams) race on it: serialise them. */
 #define HGEMM_SM100_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
 int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* stream);
+
+/* ------------------------------------------- tensor-parallel row scatter --
+ * The row-parallel (K-split) GEMM of a tensor-parallel layer produces one FP32
+ * partial C per GPU, and the layer's output is their sum. No counterpart in
+ * the reference (single-GPU); this replaces "FP32 GEMM, then NCCL
+ * reduce-scatter": the GEMM's epilogue writes each output row straight into
+ * the receive buffer of the GPU that owns the row (stores to peer memory over
+ * NVLink, issued tile by tile while the next tiles compute), and each owner
+ * then sums its slots (hgemm_sm100_reduce_slots). */
+#define HGEMM_SM100_MAX_RANKS 8
+
+typedef struct HgemmSm100Scatter {
+    int32_t ranks;          /* 1 .. HGEMM_SM100_MAX_RANKS                        */
+    int32_t rank;           /* this GPU's rank                                   */
+    int64_t rows_per_rank;  /* m == ranks * rows_per_rank; rank q owns rows
+                               [q * rows_per_rank, (q + 1) * rows_per_rank)      */
+    int64_t ld_dest;        /* row pitch of every receive buffer, floats (>= n)  */
+    void* dest[HGEMM_SM100_MAX_RANKS];
+                            /* receive buffer of each rank as mapped in this
+                               process (dest[rank] local, the others peer
+                               mappings, see hgemm_sm100_ipc_open): FP32
+                               [ranks][rows_per_rank][ld_dest], slot s written
+                               by rank s                                         */
+} HgemmSm100Scatter;
+
+/* hgemm_sm100_run with the row scatter: args->flags must include
+ * HGEMM_SM100_FLAG_OUT_F32 and args->epilogue must be 0; args->c / ldc are
+ * not written (pass any valid pointer and ldc >= n). Output row i (of m)
+ * goes to dest[q] + ((rank * rows_per_rank) + i - q * rows_per_rank) * ld_dest,
+ * q = i / rows_per_rank. The kernel waits for no other GPU: the caller orders
+ * every owner's reduction after all ranks' GEMMs (a collective on the stream,
+ * for example), and a receive buffer is not rewritten before its owner has
+ * reduced it (double-buffer across steps). */
+int hgemm_sm100_run_scatter(const HgemmSm100Args* args, const HgemmSm100Scatter* scatter, void* stream);
+
+/* out[j, c] = FP16(sum of slots[s][j][c] over s = 0 .. ranks-1, added in that
+ * order in FP32, one rounding), j < rows, c < cols. slots: FP32
+ * [ranks][rows][ld_slots], out: FP16 [rows][ld_out], device memory. */
+int hgemm_sm100_reduce_slots(const void* slots, int32_t ranks, int64_t rows, int64_t cols, int64_t ld_slots,
+                             void* out, int64_t ld_out, void* stream);
+
+/* Device memory on the current device whose CUDA IPC handle maps exactly this
+ * range in another process of the node (a whole cudaMalloc allocation). */
+int hgemm_sm100_alloc_shared(uint64_t bytes, void** ptr_out);
+int hgemm_sm100_free_shared(void* ptr);
+/* 64-byte IPC handle of an hgemm_sm100_alloc_shared pointer; mapping of a
+ * peer's handle in this process (peer access enabled), and its release. */
+int hgemm_sm100_ipc_handle(const void* ptr, void* handle_out);
+int hgemm_sm100_ipc_open(const void* handle, void** ptr_out);
+int hgemm_sm100_ipc_close(void* ptr);
 
 /* Human-readable text of a status code. */
 const char* hgemm_sm100_status_string(int status);

@@ -71,17 +71,153 @@ struct GemmParams {
     unsigned long long* flags;
     unsigned long long epoch;  // this launch's flag value (never 0)
     int streamk;               // 1: stream-K k-ranges, 0: whole tiles
+    // Fused epilogue (kEpi* bits; 0 = plain store). Applied once, by whoever
+    // stores the final FP32 sum of an output element: split-K and stream-K
+    // partials stay raw.
+    int epi;
+    int epi_vec;               // bias and residual 16-byte aligned, ldr % 8 == 0
+    const __half* bias;        // [n] (kEpiBias), indexed by accumulator column
+    const __half* residual;    // [m, ldr] (kEpiResidual)
+    long long ldr;
+    // Row scatter of an FP32 partial (tensor-parallel down-projection): with
+    // sc_ranks > 0, output row i goes to slot sc_rank of the receive buffer of
+    // rank q = i / sc_rows, sc_dest[q] (a peer GPU's memory for q != sc_rank),
+    // at row i - q * sc_rows of that slot.
+    int sc_ranks, sc_rank, sc_rows;
+    long long sc_ld;
+    float* sc_dest[8];
 };
 
+// Epilogue bits. With kEpiSiluMul the accumulator columns come in (gate, up)
+// pairs 2j, 2j + 1 and output column j = silu(gate) * up: C is [m, n / 2].
+constexpr int kEpiBias = 1;
+constexpr int kEpiResidual = 2;
+constexpr int kEpiSiluMul = 4;
+
+// Start of FP32 output row `row` (< m): C, or its scatter destination.
+__device__ __forceinline__ float* f32_row(const GemmParams& p, int row) {
+    if (p.sc_ranks > 0) {
+        const int q = row / p.sc_rows;
+        return p.sc_dest[q] + (static_cast<long long>(p.sc_rank) * p.sc_rows + (row - q * p.sc_rows)) * p.sc_ld;
+    }
+    return static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc;
+}
+
 // ------------------------------------------------------------ epilogue ----
+
+// silu(g) * u = g / (1 + e^-g) * u in FP32 (for g -> -inf the quotient goes to
+// -0, as the limit does).
+__device__ __forceinline__ float silu_mul(float g, float u) { return __fdividef(g, 1.f + __expf(-g)) * u; }
+
+// Swapped tiles hold the (gate, up) columns of one output column in lanes
+// 2i (gate) and 2i + 1 (up), rows j in registers. For the row pair (j, j + 1)
+// held as (v0, v1), one exchange gives the even lane (gate, up) of row j and
+// the odd lane (gate, up) of row j + 1. Called by all 32 lanes together.
+__device__ __forceinline__ void silu_pair(uint32_t v0, uint32_t v1, int odd, float& g, float& u) {
+    const float send = __uint_as_float(odd ? v0 : v1);
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+    g = odd ? recv : __uint_as_float(v0);
+    u = odd ? __uint_as_float(v1) : recv;
+}
+
+// Adds kCnt FP16 values src[0 .. kCnt) (only the first `avail` when not
+// `vec`) to the FP32 bit patterns v. With `vec`, src is aligned to
+// 2 * kCnt bytes (16 at most): one 8-byte load for kCnt = 4, 16-byte loads
+// for multiples of 8.
+template <int kCnt>
+__device__ __forceinline__ void add_halves(const __half* src, bool vec, int avail, uint32_t* v) {
+    static_assert(kCnt == 4 || kCnt % 8 == 0, "segment of 4 or a multiple of 8 columns");
+    if (vec) {
+        if constexpr (kCnt == 4) {
+            const uint2 q = __ldg(reinterpret_cast<const uint2*>(src));
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&q.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&q.y));
+            v[0] = __float_as_uint(__uint_as_float(v[0]) + f0.x);
+            v[1] = __float_as_uint(__uint_as_float(v[1]) + f0.y);
+            v[2] = __float_as_uint(__uint_as_float(v[2]) + f1.x);
+            v[3] = __float_as_uint(__uint_as_float(v[3]) + f1.y);
+        } else {
+#pragma unroll
+            for (int i = 0; i < kCnt; i += 8) {
+                const uint4 q = __ldg(reinterpret_cast<const uint4*>(src + i));
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+                    v[i + 2 * j] = __float_as_uint(__uint_as_float(v[i + 2 * j]) + f.x);
+                    v[i + 2 * j + 1] = __float_as_uint(__uint_as_float(v[i + 2 * j + 1]) + f.y);
+                }
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < kCnt; ++i)
+            if (i < avail) v[i] = __float_as_uint(__uint_as_float(v[i]) + __half2float(src[i]));
+    }
+}
+
+// Bias and residual terms of kCnt consecutive accumulator columns col0 .. of
+// output row `row`, added in place (no-op without those epilogue bits).
+template <int kCnt>
+__device__ __forceinline__ void epi_add_row(const GemmParams& p, int row, int col0, uint32_t* v) {
+    if ((p.epi & (kEpiBias | kEpiResidual)) == 0 || col0 >= p.n) return;
+    const bool vec = p.epi_vec && col0 + kCnt <= p.n;
+    if (p.epi & kEpiBias) add_halves<kCnt>(p.bias + col0, vec, p.n - col0, v);
+    if ((p.epi & kEpiResidual) && row < p.m)
+        add_halves<kCnt>(p.residual + static_cast<long long>(row) * p.ldr + col0, vec, p.n - col0, v);
+}
+
+// Swapped tiles: one accumulator row = output column `col`, kCnt accumulator
+// columns = output rows row0 .. row0 + kCnt - 1.
+template <int kCnt>
+__device__ __forceinline__ void epi_add_col(const GemmParams& p, int col, int row0, uint32_t* v) {
+    if ((p.epi & (kEpiBias | kEpiResidual)) == 0 || col >= p.n) return;
+    const float bias = (p.epi & kEpiBias) ? __half2float(p.bias[col]) : 0.f;
+#pragma unroll
+    for (int j = 0; j < kCnt; ++j) {
+        float x = __uint_as_float(v[j]) + bias;
+        if ((p.epi & kEpiResidual) && row0 + j < p.m)
+            x += __half2float(p.residual[static_cast<long long>(row0 + j) * p.ldr + col]);
+        v[j] = __float_as_uint(x);
+    }
+}
 
 // Stores `cnt` (16 or 32) consecutive accumulator columns of one output row.
 template <int kCnt>
 __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, int col0,
-                                                  const uint32_t* v) {
+                                                  const uint32_t* vin) {
     if (row >= p.m) return;
+    uint32_t v[kCnt];
+#pragma unroll
+    for (int i = 0; i < kCnt; ++i) v[i] = vin[i];
+    epi_add_row<kCnt>(p, row, col0, v);
+    if (p.epi & kEpiSiluMul) {
+        // col0 is a multiple of 16: output columns col0 / 2 .. (8-aligned).
+        __half* crow = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc + (col0 >> 1);
+        if (p.vec_ok && col0 + kCnt <= p.n) {
+#pragma unroll
+            for (int i = 0; i < kCnt; i += 16) {
+                uint4 q;
+                q.x = pack_half2(__float_as_uint(silu_mul(__uint_as_float(v[i + 0]), __uint_as_float(v[i + 1]))),
+                                 __float_as_uint(silu_mul(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]))));
+                q.y = pack_half2(__float_as_uint(silu_mul(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5]))),
+                                 __float_as_uint(silu_mul(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7]))));
+                q.z = pack_half2(__float_as_uint(silu_mul(__uint_as_float(v[i + 8]), __uint_as_float(v[i + 9]))),
+                                 __float_as_uint(silu_mul(__uint_as_float(v[i + 10]), __uint_as_float(v[i + 11]))));
+                q.w = pack_half2(__float_as_uint(silu_mul(__uint_as_float(v[i + 12]), __uint_as_float(v[i + 13]))),
+                                 __float_as_uint(silu_mul(__uint_as_float(v[i + 14]), __uint_as_float(v[i + 15]))));
+                *reinterpret_cast<uint4*>(crow + (i >> 1)) = q;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kCnt; i += 2)
+                if (col0 + i < p.n)
+                    crow[i >> 1] = __float2half_rn(silu_mul(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
+        }
+        return;
+    }
     if (p.out_f32) {
-        float* crow = static_cast<float*>(p.c) + static_cast<long long>(row) * p.ldc;
+        float* crow = f32_row(p, row);
         if (p.vec_ok && col0 + kCnt <= p.n) {
 #pragma unroll
             for (int i = 0; i < kCnt; i += 4)
@@ -112,28 +248,76 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
 }
 
 // Swapped tiles: accumulator row = output column `col`, accumulator columns =
-// output rows row0 .. row0 + cnt - 1.
+// output rows row0 .. row0 + cnt - 1. Called by all 32 lanes of a warp
+// together, lane l holding column col0 + l for a 32-aligned col0.
 template <int kCnt>
 __device__ __forceinline__ void store_col_segment(const GemmParams& p, int col, int row0,
-                                                  const uint32_t* v) {
+                                                  const uint32_t* vin) {
+    uint32_t v[kCnt];
+#pragma unroll
+    for (int j = 0; j < kCnt; ++j) v[j] = vin[j];
+    epi_add_col<kCnt>(p, col, row0, v);
+    if (p.epi & kEpiSiluMul) {
+        // The (gate, up) pair of output column col / 2 sits in lanes 2i, 2i + 1;
+        // of each two output rows the even lane finishes the first, the odd
+        // lane the second.
+        const int odd = col & 1;
+#pragma unroll
+        for (int j = 0; j < kCnt; j += 2) {
+            float g, u;
+            silu_pair(v[j], v[j + 1], odd, g, u);
+            const int row = row0 + j + odd;
+            if (col < p.n && row < p.m)
+                static_cast<__half*>(p.c)[static_cast<long long>(row) * p.ldc + (col >> 1)] =
+                    __float2half_rn(silu_mul(g, u));
+        }
+        return;
+    }
     if (col >= p.n) return;
 #pragma unroll
     for (int j = 0; j < kCnt; ++j) {
         const int row = row0 + j;
         if (row < p.m) {
-            const long long off = static_cast<long long>(row) * p.ldc + col;
-            if (p.out_f32) static_cast<float*>(p.c)[off] = __uint_as_float(v[j]);
-            else static_cast<__half*>(p.c)[off] = __float2half_rn(__uint_as_float(v[j]));
+            if (p.out_f32) f32_row(p, row)[col] = __uint_as_float(v[j]);
+            else static_cast<__half*>(p.c)[static_cast<long long>(row) * p.ldc + col] = __float2half_rn(__uint_as_float(v[j]));
         }
     }
 }
 
-// Stores 4 consecutive output columns of one row from an FP32 quad.
-__device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col, float4 v) {
+// Bias + residual terms of output (row, col .. col + 3) as FP32 (zero
+// without those epilogue bits or outside C); col a multiple of 4.
+__device__ __forceinline__ float4 epi_terms_quad(const GemmParams& p, int row, int col) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    epi_add_row<4>(p, row, col, w);
+    return make_float4(__uint_as_float(w[0]), __uint_as_float(w[1]), __uint_as_float(w[2]), __uint_as_float(w[3]));
+}
+
+// Stores 4 consecutive output columns of one row from an FP32 quad (col a
+// multiple of 4). With `terms_added` the caller has added the bias and
+// residual terms already (epi_terms_quad).
+__device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col, float4 v,
+                                           bool terms_added = false) {
     if (row >= p.m || col >= p.n) return;
+    if (p.epi) {
+        if (!terms_added) {
+            const float4 t = epi_terms_quad(p, row, col);
+            v.x += t.x; v.y += t.y; v.z += t.z; v.w += t.w;
+        }
+        if (p.epi & kEpiSiluMul) {
+            __half* c = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc + (col >> 1);
+            const float h0 = silu_mul(v.x, v.y), h1 = silu_mul(v.z, v.w);
+            if (p.vec_ok && col + 4 <= p.n) {
+                *reinterpret_cast<__half2*>(c) = __floats2half2_rn(h0, h1);
+            } else {
+                c[0] = __float2half_rn(h0);
+                if (col + 2 < p.n) c[1] = __float2half_rn(h1);
+            }
+            return;
+        }
+    }
     const long long off = static_cast<long long>(row) * p.ldc + col;
     if (p.out_f32) {
-        float* c = static_cast<float*>(p.c) + off;
+        float* c = f32_row(p, row) + col;
         if (p.vec_ok && col + 4 <= p.n) {
             *reinterpret_cast<float4*>(c) = v;
         } else {
@@ -190,18 +374,30 @@ __device__ __forceinline__ void store_box_tma(const CUtensorMap* map, uint8_t* b
 // n0 + l, v[j] for row m0 + j. Staged densely ([row][32] halves, 64-byte
 // rows, unswizzled map) and written by one TMA store (which clips at the
 // matrix edges). Double-buffered per warp like store_box_tma.
+// With `silu` (the SwiGLU epilogue) lanes 2i, 2i + 1 hold a (gate, up) pair:
+// the box is kRows x 16 output columns starting at n0 / 2.
 template <int kRows>
 __device__ __forceinline__ void store_box_tma_t(const CUtensorMap* map, uint8_t* box, uint32_t lane,
-                                                const uint32_t* v, int n0, int m0) {
+                                                const uint32_t* v, int n0, int m0, bool silu = false) {
     if (lane == 0) bulk_wait_group_read<1>();
     __syncwarp();
     __half* h = reinterpret_cast<__half*>(box);
+    if (silu) {
+        const int odd = static_cast<int>(lane & 1u);
 #pragma unroll
-    for (int j = 0; j < kRows; ++j) h[j * 32 + lane] = __float2half_rn(__uint_as_float(v[j]));
+        for (int j = 0; j < kRows; j += 2) {
+            float g, u;
+            silu_pair(v[j], v[j + 1], odd, g, u);
+            h[(j + odd) * 16 + (lane >> 1)] = __float2half_rn(silu_mul(g, u));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < kRows; ++j) h[j * 32 + lane] = __float2half_rn(__uint_as_float(v[j]));
+    }
     fence_async_shared();
     __syncwarp();
     if (lane == 0) {
-        tma_store_2d(map, box, n0, m0);
+        tma_store_2d(map, box, silu ? n0 / 2 : n0, m0);
         bulk_commit_group();
     }
 }
@@ -290,6 +486,41 @@ __device__ __forceinline__ uint64_t mnmaj_desc(uint32_t tile, int kk) {
 // no TMA write into this CTA's shared memory is still in flight at exit.
 // A producer that owns every kStep-th stage from `which` on (kStages a
 // multiple of kStep) and armed `issued` loads in order drains its own stages.
+// Owner side of the tensor-parallel row scatter: out[j][c] = FP16 of the FP32
+// sum of slots[s][j][c] over s = 0 .. ranks - 1, added in that order (one
+// rounding). Grid-stride over rows x column groups; kVec: cols, ld_slots and
+// ld_out multiples of 4 with 16- / 8-byte-aligned bases, one float4 per slot
+// per step. Streaming loads: the slots are read once.
+template <bool kVec>
+__global__ void __launch_bounds__(256) reduce_slots_kernel(const float* __restrict__ slots, int ranks,
+                                                           long long rows, long long cols, long long ld_slots,
+                                                           __half* __restrict__ out, long long ld_out) {
+    const long long slot_stride = rows * ld_slots;
+    const long long per_row = kVec ? cols / 4 : cols;
+    const long long total = rows * per_row;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long r = i / per_row;
+        const long long c = (i - r * per_row) * (kVec ? 4 : 1);
+        const float* src = slots + r * ld_slots + c;
+        if constexpr (kVec) {
+            float4 acc = __ldcs(reinterpret_cast<const float4*>(src));
+            for (int s = 1; s < ranks; ++s) {
+                const float4 x = __ldcs(reinterpret_cast<const float4*>(src + s * slot_stride));
+                acc.x += x.x; acc.y += x.y; acc.z += x.z; acc.w += x.w;
+            }
+            uint2 q;
+            q.x = pack_half2(__float_as_uint(acc.x), __float_as_uint(acc.y));
+            q.y = pack_half2(__float_as_uint(acc.z), __float_as_uint(acc.w));
+            *reinterpret_cast<uint2*>(out + r * ld_out + c) = q;
+        } else {
+            float acc = __ldcs(src);
+            for (int s = 1; s < ranks; ++s) acc += __ldcs(src + s * slot_stride);
+            out[r * ld_out + c] = __float2half_rn(acc);
+        }
+    }
+}
+
 template <int kStages, int kStep = 1>
 __device__ __forceinline__ void drain_tma(uint64_t* full, uint32_t issued, uint32_t which = 0) {
     constexpr uint32_t kOwn = kStages / kStep;
@@ -390,7 +621,8 @@ __device__ __forceinline__ void reduce_owned_rows(const GemmParams& p, const flo
     // Fast store path: FP16, 16-byte-aligned rows, tile inside C.
     const int rows_total = kSwap ? p.n : p.m;
     const int cols_total = kSwap ? p.m : p.n;
-    const bool fast = !p.out_f32 && p.vec_ok && acc_row0 + first + nrows <= rows_total && acc_col0 + kBNm <= cols_total;
+    const bool has_terms = (p.epi & (kEpiBias | kEpiResidual)) != 0;
+    const bool fast = !p.out_f32 && !p.epi && p.vec_ok && acc_row0 + first + nrows <= rows_total && acc_col0 + kBNm <= cols_total;
     const int quads = nrows >> 2;                         // nrows is a multiple of 4
     const int total = kSwap ? kBNm * quads : nrows * (kBNm / 4);
     for (int base = threadIdx.x; base < total; base += kU * kThreads) {
@@ -414,6 +646,13 @@ __device__ __forceinline__ void reduce_owned_rows(const GemmParams& p, const flo
             }
             acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        // Bias / residual terms, loaded together with the partials (their
+        // latency overlaps the partial loads instead of following the sum).
+        float4 terms[kU];
+        if (has_terms) {
+#pragma unroll
+            for (int u = 0; u < kU; ++u) terms[u] = epi_terms_quad(p, row[u], col[u]);
+        }
         for (int s = 0; s < split; ++s) {
             const float* rs = recv + s * rank_stride;
 #pragma unroll
@@ -432,7 +671,10 @@ __device__ __forceinline__ void reduce_owned_rows(const GemmParams& p, const flo
                 *reinterpret_cast<uint2*>(static_cast<__half*>(p.c) + static_cast<long long>(row[u]) * p.ldc +
                                           col[u]) = q;
             } else {
-                store_quad(p, row[u], col[u], acc[u]);
+                if (has_terms) {
+                    acc[u].x += terms[u].x; acc[u].y += terms[u].y; acc[u].z += terms[u].z; acc[u].w += terms[u].w;
+                }
+                store_quad(p, row[u], col[u], acc[u], true);
             }
         }
     }
@@ -636,8 +878,10 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
                     for (int c = 0; c < kBNm; c += Cfg::kChunk) {
                         uint32_t v[Cfg::kChunk];
                         tmem_ld_acc<Cfg::kChunk>(t_row + c, kBNm, two, v);
+                        epi_add_col<Cfg::kChunk>(p, acc_row0 + r, acc_col0 + c, v);
                         store_box_tma_t<Cfg::kChunk>(&tm_c, boxes + buf * 2048u, lane, v,
-                                                     acc_row0 + static_cast<int>(warp) * 32, acc_col0 + c);
+                                                     acc_row0 + static_cast<int>(warp) * 32, acc_col0 + c,
+                                                     (p.epi & kEpiSiluMul) != 0);
                         buf ^= 1u;
                     }
                 } else {
@@ -646,6 +890,8 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
                         uint32_t v0[32], v1[32];
                         tmem_ld_acc<32>(t_row + c, kBNm, two, v0);
                         tmem_ld_acc<32>(t_row + c + 32, kBNm, two, v1);
+                        epi_add_row<32>(p, acc_row0 + r, acc_col0 + c, v0);
+                        epi_add_row<32>(p, acc_row0 + r, acc_col0 + c + 32, v1);
                         store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, acc_col0 + c,
                                       acc_row0 + static_cast<int>(warp) * 32);
                         buf ^= 1u;
@@ -761,6 +1007,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
         reduce_owned_rows<kBNm, kSwap>(p, recv, split, nrows, nrows_max, sw_stride, first, acc_row0, acc_col0);
     }
 
+    if (p.sc_ranks > 0) __threadfence_system();   // peer stores of a scatter, before the grid ends
     __syncthreads();
     if (warp == 5) {
         tc_fence_after_sync();
@@ -922,6 +1169,8 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
                     tmem_ld_32x32b_x32(t_acc + c, v0);
                     tmem_ld_32x32b_x32(t_acc + c + 32, v1);
                     tmem_wait_ld();
+                    epi_add_row<32>(p, row, tn * kBN + c, v0);
+                    epi_add_row<32>(p, row, tn * kBN + c + 32, v1);
                     store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, tn * kBN + c,
                                   tm * kMmaM + warp * 32);
                     buf ^= 1u;
@@ -942,6 +1191,7 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
     }
 
     __syncwarp();
+    if (p.sc_ranks > 0) __threadfence_system();   // peer stores of a scatter, before the grid ends
     tc_fence_before_sync();
     __syncthreads();
     if (warp == 5) {
@@ -1136,6 +1386,8 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     tmem_ld_32x32b_x32(t_acc + c, v0);
                     tmem_ld_32x32b_x32(t_acc + c + 32, v1);
                     tmem_wait_ld();
+                    epi_add_row<32>(p, row0 + static_cast<int>(lane), col0 + c, v0);
+                    epi_add_row<32>(p, row0 + static_cast<int>(lane), col0 + c + 32, v1);
                     store_box_tma(&tm_c, boxes + buf * 4096u, lane, v0, v1, col0 + c, row0);
                     buf ^= 1u;
                 }
@@ -1159,6 +1411,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     // An aborted pipeline may leave the peer's copies in flight towards the
     // even CTA's barrier; give them time to land before either CTA exits.
     if (*abort_flag) settle_ns(2000000ull);
+    if (p.sc_ranks > 0) __threadfence_system();   // peer stores of a scatter, before the grid ends
     tc_fence_before_sync();
     cluster_sync();                       // no CTA leaves while its pair may still touch it
     if (warp == 5) {
@@ -1498,6 +1751,8 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                     } else {
                         tmem_wait_ld();
                     }
+                    epi_add_row<32>(p, tr * kMmaM + r, tc * kBNm + c, v0);
+                    epi_add_row<32>(p, tr * kMmaM + r, tc * kBNm + c + 32, v1);
                     store_box_tma(&tm_c, boxes + epi_buf * 4096u, lane, v0, v1, tc * kBNm + c,
                                   tr * kMmaM + warp * 32);
                     epi_buf ^= 1u;
@@ -1542,8 +1797,10 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                     }
                     if constexpr (kSwap) {
                         if (p.tma_store) {
+                            epi_add_col<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
                             store_box_tma_t<Cfg::kChunk>(&tm_c, smem + kStages * Cfg::kStageBytes + warp * 4096u + epi_buf * 2048u,
-                                                         lane, v, tr * kMmaM + static_cast<int>(warp) * 32, tc * kBNm + c);
+                                                         lane, v, tr * kMmaM + static_cast<int>(warp) * 32, tc * kBNm + c,
+                                                         (p.epi & kEpiSiluMul) != 0);
                             epi_buf ^= 1u;
                         } else {
                             store_col_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
@@ -1575,6 +1832,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     }
 
     __syncwarp();
+    if (p.sc_ranks > 0) __threadfence_system();   // peer stores of a scatter, before the grid ends
     tc_fence_before_sync();
     __syncthreads();
     if (warp == 5) {

@@ -22,6 +22,11 @@ namespace {
 
 using namespace hgemm;
 
+static_assert(kEpiBias == HGEMM_SM100_EPI_BIAS && kEpiResidual == HGEMM_SM100_EPI_RESIDUAL &&
+                  kEpiSiluMul == HGEMM_SM100_EPI_SILU_MUL,
+              "kernel epilogue bits match the C ABI");
+static_assert(sizeof(void*) != 8 || sizeof(HgemmSm100Args) == 152, "HgemmSm100Args layout (ctypes mirror)");
+
 __device__ int g_status_word;  // status word used when the caller passes none
 
 constexpr int kMaxDevices = 64;
@@ -410,13 +415,25 @@ SwapChoice swap_choice(int64_t m, int64_t n, int64_t k, int32_t split, int sms, 
     return swap_of_width(plan_tiles(m, n, k, sms, max_split, true, false, split > 0 ? split : 1).width);
 }
 
+// Columns of C: n, or n / 2 with the SwiGLU epilogue.
+int64_t out_cols(const HgemmSm100Args& a) { return (a.epilogue & HGEMM_SM100_EPI_SILU_MUL) ? a.n / 2 : a.n; }
+
 int check_args(const HgemmSm100Args* a) {
     if (a == nullptr || a->a == nullptr || a->b == nullptr || a->c == nullptr)
         return HGEMM_SM100_ERR_INVALID_ARGUMENT;
     if (a->m <= 0 || a->n <= 0 || a->k <= 0) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
     const int64_t lim = (int64_t{1} << 31) - 1;
     if (a->m > lim || a->n > lim || a->k > lim) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
-    if (a->lda < a->k || a->ldb < a->n || a->ldc < a->n) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    const int32_t epi = a->epilogue;
+    const bool silu = (epi & HGEMM_SM100_EPI_SILU_MUL) != 0;
+    if (a->lda < a->k || a->ldb < a->n || a->ldc < out_cols(*a)) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (epi & ~(HGEMM_SM100_EPI_BIAS | HGEMM_SM100_EPI_RESIDUAL | HGEMM_SM100_EPI_SILU_MUL))
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (epi != 0 && (a->flags & HGEMM_SM100_FLAG_OUT_F32)) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if ((epi & HGEMM_SM100_EPI_BIAS) && a->bias == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if ((epi & HGEMM_SM100_EPI_RESIDUAL) && (a->residual == nullptr || a->ldr < a->n || silu))
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (silu && a->n % 2 != 0) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
     if (a->config < 0 || a->config >= HGEMM_SM100_CFG_COUNT) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
     if (a->split_k < 0 || a->split_k > kMaxSplit) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
     return HGEMM_SM100_OK;
@@ -552,7 +569,7 @@ Staging plan_staging(const HgemmSm100Args& a) {
         off = align_up(off + static_cast<size_t>(a.k) * st.ldb * 2, kStageAlign);
     }
     if (st.c) {
-        st.ldc = static_cast<int64_t>(align_up(a.n, 8));
+        st.ldc = static_cast<int64_t>(align_up(out_cols(a), 8));
         st.off_c = off;
         off = align_up(off + static_cast<size_t>(a.m) * st.ldc * 2, kStageAlign);
     }
@@ -724,7 +741,8 @@ int launch_copy(const __half* src, int64_t ld_src, __half* dst, int64_t ld_dst, 
 // Launches the resolved configuration on operands that TMA can describe
 // (or, for the generic configuration, on any operands).
 int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceInfo& dev, int devid,
-             cudaStream_t stream, uint8_t* region, size_t region_bytes) {
+             cudaStream_t stream, uint8_t* region, size_t region_bytes,
+             const HgemmSm100Scatter* sc = nullptr) {
     int rc = HGEMM_SM100_OK;
     GemmParams p{};
     p.a = static_cast<const __half*>(a.a);
@@ -742,6 +760,26 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
     p.inject = (a.flags & HGEMM_SM100_FLAG_TEST_INJECT_TX) ? 1 : 0;
     p.status = a.status != nullptr ? a.status : dev.status_word;
     p.timeout_ns = a.timeout_ns != 0 ? a.timeout_ns : kDefaultTimeoutNs;
+    p.epi = a.epilogue;
+    p.bias = static_cast<const __half*>(a.bias);
+    p.residual = static_cast<const __half*>(a.residual);
+    p.ldr = a.ldr;
+    if (sc != nullptr) {
+        p.sc_ranks = sc->ranks;
+        p.sc_rank = sc->rank;
+        p.sc_rows = static_cast<int>(sc->rows_per_rank);
+        p.sc_ld = sc->ld_dest;
+        bool aligned = sc->ld_dest % 8 == 0;
+        for (int q = 0; q < sc->ranks; ++q) {
+            p.sc_dest[q] = static_cast<float*>(sc->dest[q]);
+            aligned = aligned && reinterpret_cast<uintptr_t>(sc->dest[q]) % 16 == 0;
+        }
+        p.vec_ok = aligned;
+    }
+    p.epi_vec = (p.epi & HGEMM_SM100_EPI_BIAS ? reinterpret_cast<uintptr_t>(a.bias) % 16 == 0 : true) &&
+                (p.epi & HGEMM_SM100_EPI_RESIDUAL
+                     ? reinterpret_cast<uintptr_t>(a.residual) % 16 == 0 && a.ldr % 8 == 0
+                     : true);
 
     CUtensorMap map_k, map_mn, map_c;
     std::memset(&map_k, 0, sizeof(map_k));
@@ -750,10 +788,13 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
     // TMA-store epilogue (persistent and pair kernels): FP16 C whose base and
     // pitch TMA can describe; boxes of 32 rows x 64 columns.
     // Swapped tile kernels store [kChunk rows x 32 columns] boxes, unswizzled.
+    // With the SwiGLU epilogue (half-width C) only the swapped tiles (box_cols
+    // 32 -> 16 output columns) use TMA stores; the others store from registers.
     auto prepare_store = [&](uint32_t box_cols = 64, uint32_t box_rows = 32, bool swizzle = true) -> int {
-        if (!p.vec_ok || p.out_f32) return HGEMM_SM100_OK;
-        const int r = tensor_map(&map_c, a.c, static_cast<uint64_t>(a.n), static_cast<uint64_t>(a.m),
-                                 static_cast<uint64_t>(a.ldc), box_cols, box_rows, swizzle);
+        const bool silu = (p.epi & HGEMM_SM100_EPI_SILU_MUL) != 0;
+        if (!p.vec_ok || p.out_f32 || (silu && box_cols != 32)) return HGEMM_SM100_OK;
+        const int r = tensor_map(&map_c, a.c, static_cast<uint64_t>(out_cols(a)), static_cast<uint64_t>(a.m),
+                                 static_cast<uint64_t>(a.ldc), silu ? box_cols / 2 : box_cols, box_rows, swizzle);
         if (r == HGEMM_SM100_OK) p.tma_store = 1;
         return r;
     };
@@ -875,7 +916,9 @@ extern "C" int hgemm_sm100_resolve(const HgemmSm100Args* args, int32_t* config_o
     return resolve(*args, *dev, config_out, split_out);
 }
 
-extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
+namespace {
+
+int run_impl(const HgemmSm100Args* args, const HgemmSm100Scatter* sc, void* stream_ptr) {
     int rc = check_args(args);
     if (rc != HGEMM_SM100_OK) return rc;
     const DeviceInfo* dev = nullptr;
@@ -903,7 +946,7 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
         region_bytes = static_cast<size_t>(args->workspace_bytes) - region_off;
     }
 
-    if (!staged) return run_core(*args, cfg, split, *dev, devid, stream, region, region_bytes);
+    if (!staged) return run_core(*args, cfg, split, *dev, devid, stream, region, region_bytes, sc);
 
     // Stage, run on the staged operands, copy a staged C back.
     HgemmSm100Args s = *args;
@@ -929,11 +972,90 @@ extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
     }
     s.config = cfg;
     s.split_k = split;
-    if ((rc = run_core(s, cfg, split, *dev, devid, stream, region, region_bytes)) != HGEMM_SM100_OK) return rc;
+    if ((rc = run_core(s, cfg, split, *dev, devid, stream, region, region_bytes, sc)) != HGEMM_SM100_OK) return rc;
     if (st.c)
         return launch_copy(static_cast<const __half*>(s.c), st.ldc, static_cast<__half*>(args->c), args->ldc,
-                           args->m, args->n, false, dev->sms, stream);
+                           args->m, out_cols(*args), false, dev->sms, stream);
     return HGEMM_SM100_OK;
+}
+
+}  // namespace
+
+extern "C" int hgemm_sm100_run(const HgemmSm100Args* args, void* stream_ptr) {
+    return run_impl(args, nullptr, stream_ptr);
+}
+
+// ============================================== tensor-parallel row scatter ==
+
+extern "C" int hgemm_sm100_run_scatter(const HgemmSm100Args* args, const HgemmSm100Scatter* sc,
+                                       void* stream_ptr) {
+    if (args == nullptr || sc == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (!(args->flags & HGEMM_SM100_FLAG_OUT_F32) || args->epilogue != 0) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (sc->ranks < 1 || sc->ranks > HGEMM_SM100_MAX_RANKS || sc->rank < 0 || sc->rank >= sc->ranks)
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    if (sc->rows_per_rank <= 0 || sc->rows_per_rank * sc->ranks != args->m || sc->ld_dest < args->n)
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    for (int q = 0; q < sc->ranks; ++q)
+        if (sc->dest[q] == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    return run_impl(args, sc, stream_ptr);
+}
+
+extern "C" int hgemm_sm100_reduce_slots(const void* slots, int32_t ranks, int64_t rows, int64_t cols,
+                                        int64_t ld_slots, void* out, int64_t ld_out, void* stream_ptr) {
+    if (slots == nullptr || out == nullptr || ranks < 1 || ranks > HGEMM_SM100_MAX_RANKS || rows <= 0 ||
+        cols <= 0 || ld_slots < cols || ld_out < cols)
+        return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    const DeviceInfo* dev = nullptr;
+    const int rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    const bool vec = cols % 4 == 0 && ld_slots % 4 == 0 && ld_out % 4 == 0 &&
+                     reinterpret_cast<uintptr_t>(slots) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0;
+    const int64_t items = rows * (vec ? cols / 4 : cols);
+    // HBM-bound: 8 blocks of 256 threads per SM, grid-stride.
+    int64_t blocks = cdiv(items, 256);
+    if (blocks > static_cast<int64_t>(dev->sms) * 8) blocks = static_cast<int64_t>(dev->sms) * 8;
+    cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+    const float* src = static_cast<const float*>(slots);
+    __half* dst = static_cast<__half*>(out);
+    if (vec)
+        reduce_slots_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, ranks, rows, cols,
+                                                                                    ld_slots, dst, ld_out);
+    else
+        reduce_slots_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, ranks, rows, cols,
+                                                                                     ld_slots, dst, ld_out);
+    return cudaGetLastError() == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
+}
+
+extern "C" int hgemm_sm100_alloc_shared(uint64_t bytes, void** ptr_out) {
+    if (ptr_out == nullptr || bytes == 0) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    *ptr_out = nullptr;
+    return cudaMalloc(ptr_out, bytes) == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_CUDA;
+}
+
+extern "C" int hgemm_sm100_free_shared(void* ptr) {
+    return cudaFree(ptr) == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_CUDA;
+}
+
+extern "C" int hgemm_sm100_ipc_handle(const void* ptr, void* handle_out) {
+    if (ptr == nullptr || handle_out == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "64-byte IPC handle");
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    std::memcpy(handle_out, &h, sizeof(h));
+    return HGEMM_SM100_OK;
+}
+
+extern "C" int hgemm_sm100_ipc_open(const void* handle, void** ptr_out) {
+    if (handle == nullptr || ptr_out == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    *ptr_out = nullptr;
+    return cudaIpcOpenMemHandle(ptr_out, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? HGEMM_SM100_OK
+                                                                                          : HGEMM_SM100_ERR_CUDA;
+}
+
+extern "C" int hgemm_sm100_ipc_close(void* ptr) {
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_CUDA;
 }
 
 extern "C" size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args) {

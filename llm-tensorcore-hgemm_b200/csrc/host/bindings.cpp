@@ -9,9 +9,10 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "B200 (sm_100a) tcgen05 HGEMM backends";
     m.def("hgemm", &hgemm, py::arg("a"), py::arg("b"), py::arg("implementation") = "auto",
-          py::arg("epilogue") = "none");
+          py::arg("epilogue") = "none", py::arg("bias") = py::none(), py::arg("residual") = py::none());
     m.def("hgemm_out", &hgemm_out, py::arg("a"), py::arg("b"), py::arg("out"),
-          py::arg("implementation"), py::arg("epilogue") = "none");
+          py::arg("implementation"), py::arg("epilogue") = "none", py::arg("bias") = py::none(),
+          py::arg("residual") = py::none());
     m.def("has_cutlass", &has_cutlass);
     m.def("backend_info", &backend_info, py::arg("implementation"));
     m.def("hgemm_out_f32", &hgemm_out_f32, py::arg("a"), py::arg("b"), py::arg("out"),

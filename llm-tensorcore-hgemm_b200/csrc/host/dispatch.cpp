@@ -10,14 +10,70 @@
 namespace {
 
 void validate_output(const torch::Tensor& out, const HgemmProblem& problem, const torch::Tensor& a,
-                     torch::ScalarType dtype, const char* dtype_name) {
+                     torch::ScalarType dtype, const char* dtype_name, int64_t out_cols) {
     TORCH_CHECK(out.is_cuda(), "out must be a CUDA tensor");
     TORCH_CHECK(out.device() == a.device(), "out must be on the same CUDA device as a and b");
     TORCH_CHECK(out.scalar_type() == dtype, "out must have dtype ", dtype_name);
     TORCH_CHECK(out.dim() == 2, "out must be two-dimensional");
-    TORCH_CHECK(out.size(0) == problem.m && out.size(1) == problem.n, "out must have shape [",
-                problem.m, ", ", problem.n, "]");
+    TORCH_CHECK(out.size(0) == problem.m && out.size(1) == out_cols, "out must have shape [",
+                problem.m, ", ", out_cols, "]");
     TORCH_CHECK(out.is_contiguous(), "out must be contiguous row-major");
+}
+
+// Fused epilogue: the name's terms joined by '+' (each at most once), and the
+// operand tensors they need.
+struct Epilogue {
+    int32_t bits = 0;
+    torch::Tensor bias, residual;
+};
+
+Epilogue parse_epilogue(const std::string& name, const HgemmProblem& p, const torch::Tensor& a,
+                        const std::optional<torch::Tensor>& bias, const std::optional<torch::Tensor>& residual) {
+    Epilogue e;
+    if (name != "none") {
+        size_t start = 0;
+        while (true) {
+            const size_t end = name.find('+', start);
+            const std::string term = name.substr(start, end == std::string::npos ? std::string::npos : end - start);
+            const int32_t bit = term == "bias"       ? HGEMM_SM100_EPI_BIAS
+                                : term == "residual" ? HGEMM_SM100_EPI_RESIDUAL
+                                : term == "silu_mul" ? HGEMM_SM100_EPI_SILU_MUL
+                                                     : 0;
+            TORCH_CHECK(bit != 0 && !(e.bits & bit), "unsupported HGEMM epilogue '", name,
+                        "' (none, bias, residual, bias+residual, silu_mul, bias+silu_mul)");
+            e.bits |= bit;
+            if (end == std::string::npos) break;
+            start = end + 1;
+        }
+        TORCH_CHECK(!((e.bits & HGEMM_SM100_EPI_RESIDUAL) && (e.bits & HGEMM_SM100_EPI_SILU_MUL)),
+                    "unsupported HGEMM epilogue '", name, "': residual does not combine with silu_mul");
+    }
+    const bool want_bias = e.bits & HGEMM_SM100_EPI_BIAS, want_res = e.bits & HGEMM_SM100_EPI_RESIDUAL;
+    TORCH_CHECK(want_bias == bias.has_value(), want_bias ? "epilogue '" + name + "' needs a bias tensor"
+                                                         : "bias given but epilogue '" + name + "' has no bias term");
+    TORCH_CHECK(want_res == residual.has_value(),
+                want_res ? "epilogue '" + name + "' needs a residual tensor"
+                         : "residual given but epilogue '" + name + "' has no residual term");
+    if (want_bias) {
+        const torch::Tensor& t = *bias;
+        TORCH_CHECK(t.is_cuda() && t.device() == a.device(), "bias must be on the same CUDA device as a and b");
+        TORCH_CHECK(t.scalar_type() == torch::kFloat16, "bias must have dtype torch.float16");
+        TORCH_CHECK(t.dim() == 1 && t.size(0) == p.n && t.is_contiguous(), "bias must be a contiguous [", p.n,
+                    "] tensor");
+        e.bias = t;
+    }
+    if (want_res) {
+        const torch::Tensor& t = *residual;
+        TORCH_CHECK(t.is_cuda() && t.device() == a.device(), "residual must be on the same CUDA device as a and b");
+        TORCH_CHECK(t.scalar_type() == torch::kFloat16, "residual must have dtype torch.float16");
+        TORCH_CHECK(t.dim() == 2 && t.size(0) == p.m && t.size(1) == p.n && t.stride(1) == 1 &&
+                        t.stride(0) >= p.n,
+                    "residual must be a [", p.m, ", ", p.n, "] tensor with unit column stride");
+        e.residual = t;
+    }
+    if (e.bits & HGEMM_SM100_EPI_SILU_MUL)
+        TORCH_CHECK(p.n % 2 == 0, "epilogue silu_mul needs an even N (gate/up column pairs), got N=", p.n);
+    return e;
 }
 
 int32_t config_id(const std::string& implementation) {
@@ -49,10 +105,17 @@ HgemmSm100Args make_args(const torch::Tensor& a, const torch::Tensor& b, const t
 }
 
 void run(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, const HgemmProblem& p,
-         int32_t cfg, int32_t flags) {
+         int32_t cfg, int32_t flags, const Epilogue& epi = Epilogue{}) {
     const c10::cuda::CUDAGuard device_guard(a.device());
     const cudaStream_t stream = c10::cuda::getCurrentCUDAStream(p.device).stream();
     HgemmSm100Args args = make_args(a, b, out, p, cfg, flags);
+    args.epilogue = epi.bits;
+    if (epi.bits & HGEMM_SM100_EPI_SILU_MUL) args.ldc = p.n / 2;
+    if (epi.bias.defined()) args.bias = epi.bias.data_ptr();
+    if (epi.residual.defined()) {
+        args.residual = epi.residual.data_ptr();
+        args.ldr = epi.residual.stride(0);
+    }
     // Operands TMA cannot describe (offset views; pitches not a multiple of 8
     // halves) are staged in a workspace from the caching allocator. It is
     // allocated on the current stream, so its reuse is stream-ordered after
@@ -72,26 +135,30 @@ void run(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor& out, con
 }  // namespace
 
 torch::Tensor hgemm(const torch::Tensor& a, const torch::Tensor& b, const std::string& implementation,
-                    const std::string& epilogue) {
+                    const std::string& epilogue, const std::optional<torch::Tensor>& bias,
+                    const std::optional<torch::Tensor>& residual) {
     const auto problem = validate_hgemm_inputs(a, b);
-    auto out = torch::empty({problem.m, problem.n}, a.options());
-    hgemm_out(a, b, out, implementation, epilogue);
+    const bool silu = epilogue.find("silu_mul") != std::string::npos;
+    auto out = torch::empty({problem.m, silu && problem.n % 2 == 0 ? problem.n / 2 : problem.n}, a.options());
+    hgemm_out(a, b, out, implementation, epilogue, bias, residual);
     return out;
 }
 
 void hgemm_out(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor out,
-               const std::string& implementation, const std::string& epilogue) {
+               const std::string& implementation, const std::string& epilogue,
+               const std::optional<torch::Tensor>& bias, const std::optional<torch::Tensor>& residual) {
     const auto problem = validate_hgemm_inputs(a, b);
-    validate_output(out, problem, a, torch::kFloat16, "torch.float16");
-    TORCH_CHECK(epilogue == "none", "HGEMM supports only epilogue='none'");
+    const Epilogue epi = parse_epilogue(epilogue, problem, a, bias, residual);
+    validate_output(out, problem, a, torch::kFloat16, "torch.float16",
+                    (epi.bits & HGEMM_SM100_EPI_SILU_MUL) ? problem.n / 2 : problem.n);
     const int32_t cfg = config_id(implementation);
-    run(a, b, out, problem, cfg, 0);
+    run(a, b, out, problem, cfg, 0, epi);
 }
 
 void hgemm_out_f32(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor out,
                    const std::string& implementation) {
     const auto problem = validate_hgemm_inputs(a, b);
-    validate_output(out, problem, a, torch::kFloat32, "torch.float32");
+    validate_output(out, problem, a, torch::kFloat32, "torch.float32", problem.n);
     const int32_t cfg = config_id(implementation);
     run(a, b, out, problem, cfg, HGEMM_SM100_FLAG_OUT_F32);
 }

@@ -5,6 +5,7 @@
 
 #include <cstdint>
 #include <map>
+#include <optional>
 #include <string>
 #include <tuple>
 
@@ -20,13 +21,17 @@ struct HgemmProblem {
 // Reference csrc/contract.cpp:3-22 (same checks, same messages).
 HgemmProblem validate_hgemm_inputs(const torch::Tensor& a, const torch::Tensor& b);
 
-// Reference csrc/dispatch.cpp:37-44.
+// Reference csrc/dispatch.cpp:37-44. `epilogue` extends the reference's
+// "none"-only argument: "bias", "residual", "bias+residual", "silu_mul",
+// "bias+silu_mul" (the operand tensors are passed as bias / residual).
 torch::Tensor hgemm(const torch::Tensor& a, const torch::Tensor& b,
-                    const std::string& implementation, const std::string& epilogue);
+                    const std::string& implementation, const std::string& epilogue,
+                    const std::optional<torch::Tensor>& bias, const std::optional<torch::Tensor>& residual);
 
 // Reference csrc/dispatch.cpp:47-96.
 void hgemm_out(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor out,
-               const std::string& implementation, const std::string& epilogue);
+               const std::string& implementation, const std::string& epilogue,
+               const std::optional<torch::Tensor>& bias, const std::optional<torch::Tensor>& residual);
 
 // FP32-output variant for tensor-parallel K-split partials (no reference
 // counterpart: the reference is single-GPU).

@@ -40,6 +40,11 @@ CFG_PAIR_128x128 = 12
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2
 
+# Fused-epilogue bits (HGEMM_SM100_EPI_*).
+EPI_BIAS = 1
+EPI_RESIDUAL = 2
+EPI_SILU_MUL = 4
+
 
 class HgemmSm100Args(ctypes.Structure):
     _fields_ = [
@@ -59,6 +64,25 @@ class HgemmSm100Args(ctypes.Structure):
         ("timeout_ns", ctypes.c_uint64),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_uint64),
+        ("epilogue", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("bias", ctypes.c_void_p),
+        ("residual", ctypes.c_void_p),
+        ("ldr", ctypes.c_int64),
+    ]
+
+
+MAX_RANKS = 8
+
+
+class HgemmSm100Scatter(ctypes.Structure):
+    """Mirror of ``HgemmSm100Scatter`` (tensor-parallel row scatter)."""
+    _fields_ = [
+        ("ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("rows_per_rank", ctypes.c_int64),
+        ("ld_dest", ctypes.c_int64),
+        ("dest", ctypes.c_void_p * MAX_RANKS),
     ]
 
 
@@ -92,6 +116,23 @@ def load() -> ctypes.CDLL:
         lib.hgemm_sm100_status_string.restype = ctypes.c_char_p
         lib.hgemm_sm100_read_status.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.c_int]
         lib.hgemm_sm100_read_status.restype = ctypes.c_int
+        lib.hgemm_sm100_run_scatter.argtypes = [ctypes.POINTER(HgemmSm100Args),
+                                                ctypes.POINTER(HgemmSm100Scatter), ctypes.c_void_p]
+        lib.hgemm_sm100_run_scatter.restype = ctypes.c_int
+        lib.hgemm_sm100_reduce_slots.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                                 ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+                                                 ctypes.c_int64, ctypes.c_void_p]
+        lib.hgemm_sm100_reduce_slots.restype = ctypes.c_int
+        lib.hgemm_sm100_alloc_shared.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
+        lib.hgemm_sm100_alloc_shared.restype = ctypes.c_int
+        lib.hgemm_sm100_free_shared.argtypes = [ctypes.c_void_p]
+        lib.hgemm_sm100_free_shared.restype = ctypes.c_int
+        lib.hgemm_sm100_ipc_handle.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.hgemm_sm100_ipc_handle.restype = ctypes.c_int
+        lib.hgemm_sm100_ipc_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+        lib.hgemm_sm100_ipc_open.restype = ctypes.c_int
+        lib.hgemm_sm100_ipc_close.argtypes = [ctypes.c_void_p]
+        lib.hgemm_sm100_ipc_close.restype = ctypes.c_int
         _lib = lib
     return _lib
 
@@ -100,11 +141,16 @@ def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
               lda: int | None = None, ldb: int | None = None, ldc: int | None = None,
               config: int = CFG_AUTO, split_k: int = 0, flags: int = 0,
               status_ptr: int | None = None, timeout_ns: int = 0,
-              workspace_ptr: int | None = None, workspace_bytes: int = 0) -> HgemmSm100Args:
+              workspace_ptr: int | None = None, workspace_bytes: int = 0,
+              epilogue: int = 0, bias_ptr: int | None = None, residual_ptr: int | None = None,
+              ldr: int | None = None) -> HgemmSm100Args:
+    if ldc is None:
+        ldc = n // 2 if epilogue & EPI_SILU_MUL else n
     return HgemmSm100Args(a_ptr, b_ptr, c_ptr, m, n, k,
                           k if lda is None else lda, n if ldb is None else ldb,
-                          n if ldc is None else ldc, config, split_k, flags,
-                          status_ptr, timeout_ns, workspace_ptr, workspace_bytes)
+                          ldc, config, split_k, flags,
+                          status_ptr, timeout_ns, workspace_ptr, workspace_bytes,
+                          epilogue, 0, bias_ptr, residual_ptr, n if ldr is None else ldr)
 
 
 def run(args: HgemmSm100Args, stream: int = 0) -> int:
@@ -134,3 +180,55 @@ def read_status(clear: bool = True) -> tuple[int, int]:
     v = ctypes.c_int32(0)
     rc = load().hgemm_sm100_read_status(ctypes.byref(v), 1 if clear else 0)
     return rc, v.value
+
+
+# ------------------------------------------- tensor-parallel row scatter --
+
+def make_scatter(ranks: int, rank: int, rows_per_rank: int, ld_dest: int, dest: list[int]) -> HgemmSm100Scatter:
+    if len(dest) != ranks or ranks > MAX_RANKS:
+        raise ValueError("one destination per rank, at most 8 ranks")
+    arr = (ctypes.c_void_p * MAX_RANKS)(*dest, *([None] * (MAX_RANKS - ranks)))
+    return HgemmSm100Scatter(ranks, rank, rows_per_rank, ld_dest, arr)
+
+
+def run_scatter(args: HgemmSm100Args, scatter: HgemmSm100Scatter, stream: int = 0) -> int:
+    return load().hgemm_sm100_run_scatter(ctypes.byref(args), ctypes.byref(scatter), ctypes.c_void_p(stream))
+
+
+def reduce_slots(slots_ptr: int, ranks: int, rows: int, cols: int, ld_slots: int, out_ptr: int, ld_out: int,
+                 stream: int = 0) -> int:
+    return load().hgemm_sm100_reduce_slots(slots_ptr, ranks, rows, cols, ld_slots, out_ptr, ld_out,
+                                           ctypes.c_void_p(stream))
+
+
+def _checked(rc: int, what: str) -> None:
+    if rc != OK:
+        raise RuntimeError(f"{what} failed: {status_string(rc)}")
+
+
+def alloc_shared(nbytes: int) -> int:
+    p = ctypes.c_void_p()
+    _checked(load().hgemm_sm100_alloc_shared(nbytes, ctypes.byref(p)), "hgemm_sm100_alloc_shared")
+    return p.value
+
+
+def free_shared(ptr: int) -> None:
+    _checked(load().hgemm_sm100_free_shared(ptr), "hgemm_sm100_free_shared")
+
+
+def ipc_handle(ptr: int) -> bytes:
+    buf = ctypes.create_string_buffer(64)
+    _checked(load().hgemm_sm100_ipc_handle(ptr, buf), "hgemm_sm100_ipc_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    if len(handle) != 64:
+        raise ValueError("IPC handles are 64 bytes")
+    p = ctypes.c_void_p()
+    _checked(load().hgemm_sm100_ipc_open(handle, ctypes.byref(p)), "hgemm_sm100_ipc_open")
+    return p.value
+
+
+def ipc_close(ptr: int) -> None:
+    _checked(load().hgemm_sm100_ipc_close(ptr), "hgemm_sm100_ipc_close")

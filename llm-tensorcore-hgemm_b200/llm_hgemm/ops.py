@@ -28,10 +28,24 @@ def hgemm(
     *,
     implementation: str = "auto",
     epilogue: str = "none",
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Row-major FP16 C = A @ B with FP32 accumulation (reference ops.py:18-30)."""
+    """Row-major FP16 C = A @ B with FP32 accumulation (reference ops.py:18-30).
+
+    ``epilogue`` (the reference accepts only ``"none"``) fuses terms into the
+    GEMM's store, on the FP32 sum, with one FP16 rounding at the end:
+
+    * ``"bias"``: ``+ bias[j]`` (FP16 ``[N]``);
+    * ``"residual"``: ``+ residual[i, j]`` (FP16 ``[M, N]``, unit column
+      stride; it may be the output of :func:`_hgemm_out` itself);
+    * ``"bias+residual"``;
+    * ``"silu_mul"`` / ``"bias+silu_mul"`` (SwiGLU): B's columns hold (gate,
+      up) pairs ``2j, 2j + 1`` (see :func:`interleave_gate_up`) and the output
+      is ``[M, N / 2]`` with ``C[:, j] = silu(g) * u``.
+    """
     resolved = selected_implementation(a, b, implementation)
-    output = _C.hgemm(a, b, resolved, epilogue)
+    output = _C.hgemm(a, b, resolved, epilogue, bias, residual)
     if implementation == "shape_auto":
         record_selected(resolved)
     return output
@@ -44,13 +58,24 @@ def _hgemm_out(
     *,
     implementation: str,
     epilogue: str = "none",
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Benchmark seam writing into a preallocated ``out`` (reference ops.py:33-46)."""
     resolved = selected_implementation(a, b, implementation)
-    _C.hgemm_out(a, b, out, resolved, epilogue)
+    _C.hgemm_out(a, b, out, resolved, epilogue, bias, residual)
     if implementation == "shape_auto":
         record_selected(resolved)
     return out
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """``[K, 2I]`` operand for the ``silu_mul`` epilogue from the ``[K, I]``
+    gate and up operands: column ``2j`` is ``gate[:, j]``, ``2j + 1`` is
+    ``up[:, j]``."""
+    if gate.shape != up.shape or gate.dim() != 2:
+        raise ValueError("gate and up must be 2-D tensors of the same shape")
+    return torch.stack((gate, up), dim=2).reshape(gate.shape[0], 2 * gate.shape[1]).contiguous()
 
 
 def hgemm_f32_out(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,

@@ -12,9 +12,30 @@ hot path: large MLP GEMMs split where they shard naturally.
   FP32 and one conversion rounds the sum to FP16. That matches the oracle's
   FP32 accumulation followed by a single FP16 rounding.
 
-Operands are always local to each GPU; data crosses NVLink only inside NCCL.
-The GEMM callables are injectable so the partitioning and reduction logic
-runs on CPU ranks (gloo) in tests.
+* Down-projection, reduce-scatter (``down_scatter``): the same FP32 partials,
+  but ``reduce_scatter`` leaves each rank only its share of the output rows,
+  summed in FP32 and rounded once to an FP16 shard: half the bytes of the
+  all-reduce cross NVLink and each rank rounds M / G rows. With ``chunks`` >
+  1 the partial is computed in row blocks and block i is reduce-scattered on
+  a side stream while block i + 1 is computed (NCCL overlaps the GEMM). Rank
+  r then owns, of every block of M / chunks rows, the r-th 1 / G of it
+  (:meth:`TensorParallelMLP.owned_rows`), stored block after block.
+
+* Down-projection, fused GEMM + reduce-scatter (``down_p2p``): the FP32
+  partial never lands in this GPU's memory as a whole. The GEMM's epilogue
+  stores each output row straight into the receive buffer of the rank that
+  owns it (peer stores over NVLink, tile by tile while later tiles compute;
+  ``hgemm_sm100_run_scatter``); one NCCL barrier orders every rank's GEMM
+  before the owners sum their G slots in rank order and round once
+  (``hgemm_sm100_reduce_slots``). Receive buffers are this library's own
+  device allocations, mapped into the peers through CUDA IPC, two per rank
+  used alternately so a rank's next GEMM never overwrites slots its peer is
+  still reducing. Rank r owns rows [r * M / G, (r + 1) * M / G).
+
+Operands of the GEMMs are always local to each GPU; data crosses NVLink in
+NCCL and, for ``down_p2p``, in the GEMM epilogue's stores (no kernel loads a
+peer's memory). The GEMM callables are injectable so the partitioning and
+reduction logic runs on CPU ranks (gloo) in tests.
 """
 
 from __future__ import annotations
@@ -58,6 +79,56 @@ def _cuda_gemm_f32(a, b, out):
     from .ops import hgemm_f32_out
 
     return hgemm_f32_out(a, b, out, implementation="auto")
+
+
+class RowScatter:
+    """Receive buffers of the fused GEMM + reduce-scatter for one process
+    group: two local buffers of FP32 [G, rows_per_rank, cols] (allocated by
+    the kernel library, shareable through CUDA IPC) and every peer's two,
+    mapped here. Construction and :meth:`close` are collective."""
+
+    def __init__(self, rows_per_rank: int, cols: int, rank: int, world: int, group=None):
+        from . import capi
+
+        if world > capi.MAX_RANKS:
+            raise ValueError(f"at most {capi.MAX_RANKS} ranks")
+        self.rows_per_rank, self.cols, self.rank, self.world, self.group = rows_per_rank, cols, rank, world, group
+        nbytes = world * rows_per_rank * cols * 4
+        self.local = [capi.alloc_shared(nbytes) for _ in range(2)]
+        handles = [capi.ipc_handle(p) for p in self.local]
+        gathered = [None] * world
+        if world > 1:
+            dist.all_gather_object(gathered, handles, group=group)
+        else:
+            gathered[0] = handles
+        self.opened = []
+        self.dest = []
+        for b in range(2):
+            row = []
+            for q in range(world):
+                if q == rank:
+                    row.append(self.local[b])
+                else:
+                    ptr = capi.ipc_open(gathered[q][b])
+                    self.opened.append(ptr)
+                    row.append(ptr)
+            self.dest.append(row)
+        self.steps = 0
+
+    def close(self) -> None:
+        from . import capi
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)     # no peer still writes into our buffers
+        for ptr in self.opened:
+            capi.ipc_close(ptr)
+        self.opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)     # every peer has unmapped them
+        for ptr in self.local:
+            capi.free_shared(ptr)
+        self.local = []
 
 
 @dataclass
@@ -123,6 +194,89 @@ class TensorParallelMLP:
             dist.all_reduce(self.partial, op=dist.ReduceOp.SUM, group=self.group)
         self.out.copy_(self.partial)          # the single FP16 rounding
         return self.out
+
+    def owned_rows(self, chunks: int = 1) -> torch.Tensor:
+        """Global output rows of this rank's :meth:`down_scatter` shard, in
+        shard order."""
+        m = self.x.shape[0]
+        if chunks < 1 or m % (chunks * self.world) != 0:
+            raise ValueError(f"M={m} must split into {chunks} blocks of {self.world} equal row groups")
+        block, part = m // chunks, m // (chunks * self.world)
+        return torch.cat([torch.arange(c * block + self.rank * part, c * block + (self.rank + 1) * part)
+                          for c in range(chunks)])
+
+    def down_scatter(self, chunks: int = 1) -> torch.Tensor:
+        """Row-parallel down-projection with a reduce-scatter: returns this
+        rank's FP16 [M / G, hidden] shard (rows :meth:`owned_rows`)."""
+        m, hidden = self.partial.shape
+        rows = self.owned_rows(chunks)          # validates the split
+        block, part = m // chunks, rows.numel() // chunks
+        if getattr(self, "shard_f32", None) is None or self.shard_f32.shape[0] != rows.numel():
+            self.shard_f32 = torch.empty((rows.numel(), hidden), device=self.x.device, dtype=torch.float32)
+            self.shard = torch.empty((rows.numel(), hidden), device=self.x.device, dtype=torch.float16)
+        use_side = self.x.is_cuda and chunks > 1
+        if use_side and getattr(self, "comm_stream", None) is None:
+            self.comm_stream = torch.cuda.Stream(device=self.x.device)
+        main = torch.cuda.current_stream(self.x.device) if self.x.is_cuda else None
+        for c in range(chunks):
+            lo, hi = c * block, (c + 1) * block
+            self.gemm_f32(self.h[lo:hi], self.w_down, self.partial[lo:hi])
+            dst, src = self.shard_f32[c * part:(c + 1) * part], self.partial[lo:hi]
+            if self.world == 1:
+                dst.copy_(src)
+            elif use_side:
+                self.comm_stream.wait_stream(main)
+                with torch.cuda.stream(self.comm_stream):
+                    dist.reduce_scatter_tensor(dst, src, op=dist.ReduceOp.SUM, group=self.group)
+            else:
+                dist.reduce_scatter_tensor(dst, src, op=dist.ReduceOp.SUM, group=self.group)
+        if use_side:
+            main.wait_stream(self.comm_stream)
+        self.shard.copy_(self.shard_f32)      # the single FP16 rounding of the owned rows
+        return self.shard
+
+    def down_p2p(self) -> torch.Tensor:
+        """Fused GEMM + reduce-scatter over peer memory: returns this rank's
+        FP16 [M / G, hidden] shard (rows [r * M / G, (r + 1) * M / G))."""
+        from . import capi
+
+        m, hidden = self.partial.shape
+        k = self.h.shape[1]
+        if m % self.world != 0:
+            raise ValueError(f"M={m} must split into {self.world} equal row groups")
+        rows = m // self.world
+        if getattr(self, "scatter", None) is None:
+            self.scatter = RowScatter(rows, hidden, self.rank, self.world, self.group)
+            self.shard_p2p = torch.empty((rows, hidden), device=self.x.device, dtype=torch.float16)
+            self._barrier_flag = torch.zeros(1, device=self.x.device, dtype=torch.int32)
+        sc = self.scatter
+        buf = sc.steps % 2
+        stream = torch.cuda.current_stream(self.x.device).cuda_stream
+        args = capi.make_args(self.h.data_ptr(), self.w_down.data_ptr(), sc.local[buf], m, hidden, k,
+                              ldc=hidden, flags=capi.FLAG_OUT_F32)
+        need = capi.workspace_size(args)
+        if need:
+            if getattr(self, "_p2p_ws", None) is None or self._p2p_ws.numel() < need:
+                self._p2p_ws = torch.empty(need, device=self.x.device, dtype=torch.uint8)
+            args.workspace, args.workspace_bytes = self._p2p_ws.data_ptr(), need
+        rc = capi.run_scatter(args, capi.make_scatter(self.world, self.rank, rows, hidden, sc.dest[buf]), stream)
+        if rc != capi.OK:
+            raise RuntimeError(f"hgemm_sm100_run_scatter failed: {capi.status_string(rc)}")
+        if self.world > 1:
+            # Orders every rank's GEMM (its peer stores) before any owner reads.
+            dist.all_reduce(self._barrier_flag, op=dist.ReduceOp.MAX, group=self.group)
+        rc = capi.reduce_slots(sc.local[buf], self.world, rows, hidden, hidden, self.shard_p2p.data_ptr(), hidden,
+                               stream)
+        if rc != capi.OK:
+            raise RuntimeError(f"hgemm_sm100_reduce_slots failed: {capi.status_string(rc)}")
+        sc.steps += 1
+        return self.shard_p2p
+
+    def close(self) -> None:
+        """Releases the peer mappings and receive buffers (collective)."""
+        if getattr(self, "scatter", None) is not None:
+            self.scatter.close()
+            self.scatter = None
 
     def step(self) -> None:
         self.up()

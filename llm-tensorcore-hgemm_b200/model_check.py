@@ -13,7 +13,9 @@ available here, so the weights are the architecture's own random init
 Prints one JSON line: for prefill (batch 1 x 2048 tokens, last-token logits)
 and cached decode (batch 16, one token at context 2048), the logits gate of
 the swapped model against the stock model and both models' device times. The
-gate result is reported whether it passes or not.
+gate result is reported whether it passes or not. Unless ``--no-fused``, a
+second copy of the model (same seed) with fused q|k|v and gate|up
+projections (``fuse_projections``) is checked and timed the same way.
 """
 
 from __future__ import annotations
@@ -78,14 +80,21 @@ def timed(fn):
 @torch.inference_mode()
 def rollout(model, prompt, decode_prompts, decode_next):
     """Last-token logits of a prefill, and decode-step logits for a batch of
-    sequences after a cached prefill of `decode_prompts`."""
+    sequences after a cached prefill of `decode_prompts`, with their device
+    times (milliseconds)."""
     pre, t_pre = timed(lambda: model(prompt, logits_to_keep=1).logits[:, -1].clone())
     cache = model(decode_prompts, use_cache=True, logits_to_keep=1).past_key_values
     torch.cuda.synchronize()
-    dec, t_dec = timed(lambda: model(decode_next, past_key_values=cache, use_cache=True,
+    # Five decode steps (the same next tokens, the cache growing by one each
+    # time); the first step's logits are compared, the median step time kept.
+    dec, times = None, []
+    for _ in range(5):
+        out, t = timed(lambda: model(decode_next, past_key_values=cache, use_cache=True,
                                      logits_to_keep=1).logits[:, -1].clone())
+        dec = out if dec is None else dec
+        times.append(t)
     del cache
-    return pre, dec, t_pre, t_dec
+    return pre, dec, t_pre, sorted(times)[len(times) // 2]
 
 
 def main() -> None:
@@ -102,9 +111,11 @@ def main() -> None:
     p.add_argument("--context", type=int, default=2048)
     p.add_argument("--seed", type=int, default=2026)
     p.add_argument("--implementation", default="auto")
+    p.add_argument("--no-fused", action="store_true",
+                   help="skip the fused-projection variant (second model copy)")
     args = p.parse_args()
 
-    from llm_hgemm.integration import FrozenHgemmLinear, swap_linears
+    from llm_hgemm.integration import FrozenHgemmLinear, HgemmSwiGLU, fuse_projections, swap_linears
 
     model = build_model(args)
     g = torch.Generator(device="cuda").manual_seed(args.seed + 1)
@@ -122,6 +133,25 @@ def main() -> None:
     out_pre, out_dec, t_pre, t_dec = rollout(model, prompt, decode_prompts, decode_next)
     backends = sorted({str(m.last_backend) for m in adapters})
 
+    fused_result = None
+    if not args.no_fused:
+        # The same seeded weights, with fused q|k|v and gate|up (silu_mul
+        # epilogue) projections; the remaining linears through FrozenHgemmLinear.
+        del model
+        torch.cuda.empty_cache()
+        model = build_model(args)
+        counts = fuse_projections(model, args.implementation)
+        counts["linears"] = swap_linears(model, args.implementation)
+        rollout(model, prompt, decode_prompts, decode_next)   # warm-up at full size
+        f_pre, f_dec, tf_pre, tf_dec = rollout(model, prompt, decode_prompts, decode_next)
+        fused_backends = sorted({str(m.last_backend) for m in model.modules()
+                                 if isinstance(m, (FrozenHgemmLinear, HgemmSwiGLU))})
+        fused_result = {
+            "fused": counts, "executed_backends": fused_backends,
+            "prefill": {**logits_gate([f_pre], [ref_pre]), "hgemm_ms": round(tf_pre, 3)},
+            "decode": {**logits_gate([f_dec], [ref_dec]), "hgemm_ms": round(tf_dec, 3)},
+        }
+
     result = {
         "model": "Qwen3-4B architecture, random init (std 0.02), FP16",
         "layers": args.layers, "hidden": args.hidden, "vocab": args.vocab,
@@ -132,6 +162,7 @@ def main() -> None:
         "decode": {"batch": args.decode_batch, "context": args.context,
                    **logits_gate([out_dec], [ref_dec]),
                    "stock_ms": round(t_dec_ref, 3), "hgemm_ms": round(t_dec, 3)},
+        "fused_projections": fused_result,
     }
     print(json.dumps(result), flush=True)
 

@@ -45,6 +45,37 @@ def torch_reference(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
 
 
 @torch.no_grad()
+def torch_reference_epilogue(a: torch.Tensor, b: torch.Tensor, epilogue: str = "none",
+                             bias: torch.Tensor | None = None,
+                             residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Oracle of the fused epilogues (an extension: the reference accepts only
+    ``epilogue="none"``, csrc/dispatch.cpp:52). Every term is applied to the
+    FP32 product of ``torch_reference`` and the result rounded once:
+
+    * ``bias``: ``+ bias[j]``; ``residual``: ``+ residual[i, j]`` (FP16 operands
+      widened to FP32), in that order;
+    * ``silu_mul``: the product's columns are (gate, up) pairs 2j, 2j + 1 and
+      output column j is ``silu(gate) * up`` (the SwiGLU of a Qwen3 MLP,
+      ``down(silu(gate(x)) * up(x))``, without the intermediate roundings of
+      the unfused layers).
+    """
+    terms = set() if epilogue == "none" else set(epilogue.split("+"))
+    saved = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        acc = torch.mm(a.to(torch.float32), b.to(torch.float32))
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = saved
+    if "bias" in terms:
+        acc = acc + bias.to(torch.float32)
+    if "residual" in terms:
+        acc = acc + residual.to(torch.float32)
+    if "silu_mul" in terms:
+        acc = torch.nn.functional.silu(acc[:, 0::2]) * acc[:, 1::2]
+    return acc.to(torch.float16)
+
+
+@torch.no_grad()
 def error_metrics(out: torch.Tensor, reference: torch.Tensor) -> dict:
     o = out.to(torch.float32)
     r = reference.to(torch.float32)

@@ -63,6 +63,18 @@ def _worker(rank, world, port, mode, results):
         out_ref = (h.float() @ w_down.float()).half()
         ok_y = torch.equal(mlp.y, y_ref)
         d = (mlp.out.float() - out_ref.float()).abs().max().item()
+        if mode == "scatter":
+            # Reduce-scatter variants: each rank's FP16 shard holds exactly
+            # its owned rows of the same FP32-summed, once-rounded output.
+            for chunks in (1, 2):
+                shard = mlp.down_scatter(chunks).clone()
+                rows = mlp.owned_rows(chunks)
+                assert shard.shape == (m // world, hidden)
+                assert torch.equal(shard, mlp.out[rows]), chunks
+                d = max(d, (shard.float() - out_ref[rows].float()).abs().max().item())
+            owned = [None] * world
+            dist.all_gather_object(owned, mlp.owned_rows(2).tolist())
+            assert sorted(sum(owned, [])) == list(range(m))
         results[rank] = (ok_y, d, mlp.total_flops(), mlp.inter_total)
         dist.barrier()
         dist.destroy_process_group()
@@ -102,9 +114,10 @@ def test_shard_helpers():
     assert torch.equal(torch.cat([shard_rows(w, r, 4) for r in range(4)], 0), w)
 
 
+@pytest.mark.parametrize("mode", ["ok", "scatter"])
 @pytest.mark.parametrize("world", [2, 3])
-def test_tp_mlp_matches_unsharded(world):
-    results = run_ranks(world, "ok")
+def test_tp_mlp_matches_unsharded(world, mode):
+    results = run_ranks(world, mode)
     assert len(results) == world
     for rank in range(world):
         res = results[rank]
