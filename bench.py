@@ -483,12 +483,20 @@ def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict
                 "reduce_scatter_ms": timed_max(lambda: mlp.down_scatter(1), vsteps)}
     chunks = 4 if mlp.x.shape[0] % (4 * world) == 0 else 1
     variants[f"reduce_scatter_overlap{chunks}_ms"] = timed_max(lambda: mlp.down_scatter(chunks), vsteps)
+    # Fused GEMM + reduce-scatter: the GEMM epilogue stores rows into their
+    # owners' buffers over NVLink, one barrier, owners sum their slots.
+    variants["p2p_fused_reduce_scatter_ms"] = timed_max(mlp.down_p2p, vsteps)
     mlp.down()
-    shard = mlp.down_scatter(chunks)
-    rows = mlp.owned_rows(chunks).to(dev)
-    d = shard.float() - mlp.out[rows].float()
-    rel = torch.linalg.vector_norm(d) / torch.linalg.vector_norm(mlp.out[rows].float()).clamp_min(1e-12)
-    scatter_ok = bool(torch.isfinite(shard.float()).all()) and d.abs().max().item() <= 5e-2 and rel.item() <= 5e-3
+
+    def shard_ok(shard, rows):
+        ref = mlp.out[rows.to(dev)].float()
+        d = shard.float() - ref
+        rel = torch.linalg.vector_norm(d) / torch.linalg.vector_norm(ref).clamp_min(1e-12)
+        return bool(torch.isfinite(shard.float()).all()) and d.abs().max().item() <= 5e-2 and rel.item() <= 5e-3
+
+    scatter_ok = shard_ok(mlp.down_scatter(chunks), mlp.owned_rows(chunks))
+    scatter_ok = shard_ok(mlp.down_p2p(), mlp.owned_rows(1)) and scatter_ok
+    mlp.close()
     ok = mlp.check()
     okt = torch.tensor([1 if (ok and scatter_ok) else 0], device=dev)
     dist.all_reduce(okt, op=dist.ReduceOp.MIN)

@@ -247,6 +247,27 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
     }
 }
 
+// FP32 rows of a row scatter through shared memory: the warp's 32 x 32 block
+// (lane l = row row0 + l, v = its columns col0 .. col0 + 31) is transposed
+// through `box` (4 KB, element (r, c) at r * 32 + (c ^ r): conflict-free both
+// ways) so that each store instruction writes 32 consecutive floats of one
+// row: whole 128-byte lines for the stores that cross NVLink, instead of 32
+// rows' 16-byte pieces. All 32 lanes call it together.
+__device__ __forceinline__ void store_block_f32(const GemmParams& p, float* box, uint32_t lane, const uint32_t* v,
+                                                int row0, int col0) {
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 32; ++c) box[lane * 32u + (static_cast<uint32_t>(c) ^ lane)] = __uint_as_float(v[c]);
+    __syncwarp();
+    const int col = col0 + static_cast<int>(lane);
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) {
+        const int row = row0 + r;
+        if (row < p.m && col < p.n) f32_row(p, row)[col] = box[r * 32 + static_cast<int>(lane ^ static_cast<uint32_t>(r))];
+    }
+    __syncwarp();
+}
+
 // Swapped tiles: accumulator row = output column `col`, accumulator columns =
 // output rows row0 .. row0 + cnt - 1. Called by all 32 lanes of a warp
 // together, lane l holding column col0 + l for a 32-aligned col0.
@@ -1181,7 +1202,10 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(t_acc + c, v);
                     tmem_wait_ld();
-                    store_row_segment<32>(p, row, tn * kBN + c, v);
+                    if (p.sc_ranks > 0)
+                        store_block_f32(p, reinterpret_cast<float*>(boxes), lane, v, tm * kMmaM + warp * 32, tn * kBN + c);
+                    else
+                        store_row_segment<32>(p, row, tn * kBN + c, v);
                 }
             }
             tc_fence_before_sync();
@@ -1397,7 +1421,10 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(t_acc + c, v);
                     tmem_wait_ld();
-                    store_row_segment<32>(p, row0 + static_cast<int>(lane), col0 + c, v);
+                    if (p.sc_ranks > 0)
+                        store_block_f32(p, reinterpret_cast<float*>(boxes), lane, v, row0, col0 + c);
+                    else
+                        store_row_segment<32>(p, row0 + static_cast<int>(lane), col0 + c, v);
                 }
             }
             tc_fence_before_sync();
@@ -1806,6 +1833,13 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
                             store_col_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
                         }
                     } else {
+                        if constexpr (Cfg::kChunk == 32) {
+                            if (p.sc_ranks > 0) {
+                                store_block_f32(p, reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes + warp * 8192u),
+                                                lane, v, tr * kMmaM + static_cast<int>(warp) * 32, tc * kBNm + c);
+                                continue;
+                            }
+                        }
                         store_row_segment<Cfg::kChunk>(p, tr * kMmaM + r, tc * kBNm + c, v);
                     }
                 }
