@@ -231,6 +231,14 @@ int hgemm_sm100_run_scatter(const HgemmSm100Args* args, const HgemmSm100Scatter*
 int hgemm_sm100_reduce_slots(const void* slots, int32_t ranks, int64_t rows, int64_t cols, int64_t ld_slots,
                              void* out, int64_t ld_out, void* stream);
 
+/* hgemm_sm100_reduce_slots writing the same FP16 rows to n_outs (1 .. 8)
+ * destinations outs[i] (each [rows][ld_out]): with the peers' copies of the
+ * owned rows among them (peer mappings), the all-gather that completes an
+ * all-reduce. The caller orders the peers' reads after it (a collective on
+ * the stream) and their earlier reads of those rows before it. */
+int hgemm_sm100_reduce_slots_gather(const void* slots, int32_t ranks, int64_t rows, int64_t cols, int64_t ld_slots,
+                                    void* const* outs, int32_t n_outs, int64_t ld_out, void* stream);
+
 /* Device memory on the current device whose CUDA IPC handle maps exactly this
  * range in another process of the node (a whole cudaMalloc allocation). */
 int hgemm_sm100_alloc_shared(uint64_t bytes, void** ptr_out);

@@ -509,13 +509,22 @@ __device__ __forceinline__ uint64_t mnmaj_desc(uint32_t tile, int kk) {
 // multiple of kStep) and armed `issued` loads in order drains its own stages.
 // Owner side of the tensor-parallel row scatter: out[j][c] = FP16 of the FP32
 // sum of slots[s][j][c] over s = 0 .. ranks - 1, added in that order (one
-// rounding). Grid-stride over rows x column groups; kVec: cols, ld_slots and
-// ld_out multiples of 4 with 16- / 8-byte-aligned bases, one float4 per slot
-// per step. Streaming loads: the slots are read once.
+// rounding), written to every destination of `outs` (with the peers' copies
+// of these rows among them, an all-gather). Grid-stride over rows x column
+// groups; kVec: cols, ld_slots and ld_out multiples of 4 with 16- / 8-byte-
+// aligned bases, one float4 per slot per step. Streaming loads: the slots are
+// read once.
+// Up to 8 FP16 destinations of one reduction (this GPU's output and its
+// peers' copies of the same rows).
+struct SlotOutputs {
+    __half* ptr[8];
+    int count;
+};
+
 template <bool kVec>
 __global__ void __launch_bounds__(256) reduce_slots_kernel(const float* __restrict__ slots, int ranks,
                                                            long long rows, long long cols, long long ld_slots,
-                                                           __half* __restrict__ out, long long ld_out) {
+                                                           SlotOutputs outs, long long ld_out) {
     const long long slot_stride = rows * ld_slots;
     const long long per_row = kVec ? cols / 4 : cols;
     const long long total = rows * per_row;
@@ -533,11 +542,12 @@ __global__ void __launch_bounds__(256) reduce_slots_kernel(const float* __restri
             uint2 q;
             q.x = pack_half2(__float_as_uint(acc.x), __float_as_uint(acc.y));
             q.y = pack_half2(__float_as_uint(acc.z), __float_as_uint(acc.w));
-            *reinterpret_cast<uint2*>(out + r * ld_out + c) = q;
+            for (int o = 0; o < outs.count; ++o) *reinterpret_cast<uint2*>(outs.ptr[o] + r * ld_out + c) = q;
         } else {
             float acc = __ldcs(src);
             for (int s = 1; s < ranks; ++s) acc += __ldcs(src + s * slot_stride);
-            out[r * ld_out + c] = __float2half_rn(acc);
+            const __half h = __float2half_rn(acc);
+            for (int o = 0; o < outs.count; ++o) outs.ptr[o][r * ld_out + c] = h;
         }
     }
 }

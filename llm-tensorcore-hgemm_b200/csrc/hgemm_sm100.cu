@@ -1002,27 +1002,40 @@ extern "C" int hgemm_sm100_run_scatter(const HgemmSm100Args* args, const HgemmSm
 
 extern "C" int hgemm_sm100_reduce_slots(const void* slots, int32_t ranks, int64_t rows, int64_t cols,
                                         int64_t ld_slots, void* out, int64_t ld_out, void* stream_ptr) {
-    if (slots == nullptr || out == nullptr || ranks < 1 || ranks > HGEMM_SM100_MAX_RANKS || rows <= 0 ||
-        cols <= 0 || ld_slots < cols || ld_out < cols)
+    return hgemm_sm100_reduce_slots_gather(slots, ranks, rows, cols, ld_slots, &out, 1, ld_out, stream_ptr);
+}
+
+extern "C" int hgemm_sm100_reduce_slots_gather(const void* slots, int32_t ranks, int64_t rows, int64_t cols,
+                                               int64_t ld_slots, void* const* outs, int32_t n_outs, int64_t ld_out,
+                                               void* stream_ptr) {
+    if (slots == nullptr || outs == nullptr || n_outs < 1 || n_outs > HGEMM_SM100_MAX_RANKS || ranks < 1 ||
+        ranks > HGEMM_SM100_MAX_RANKS || rows <= 0 || cols <= 0 || ld_slots < cols || ld_out < cols)
         return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    SlotOutputs o{};
+    o.count = n_outs;
+    bool out_aligned = true;
+    for (int i = 0; i < n_outs; ++i) {
+        if (outs[i] == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+        o.ptr[i] = static_cast<__half*>(outs[i]);
+        out_aligned = out_aligned && reinterpret_cast<uintptr_t>(outs[i]) % 8 == 0;
+    }
     const DeviceInfo* dev = nullptr;
     const int rc = device_info(&dev);
     if (rc != HGEMM_SM100_OK) return rc;
     const bool vec = cols % 4 == 0 && ld_slots % 4 == 0 && ld_out % 4 == 0 &&
-                     reinterpret_cast<uintptr_t>(slots) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 8 == 0;
+                     reinterpret_cast<uintptr_t>(slots) % 16 == 0 && out_aligned;
     const int64_t items = rows * (vec ? cols / 4 : cols);
     // HBM-bound: 8 blocks of 256 threads per SM, grid-stride.
     int64_t blocks = cdiv(items, 256);
     if (blocks > static_cast<int64_t>(dev->sms) * 8) blocks = static_cast<int64_t>(dev->sms) * 8;
     cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
     const float* src = static_cast<const float*>(slots);
-    __half* dst = static_cast<__half*>(out);
     if (vec)
         reduce_slots_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, ranks, rows, cols,
-                                                                                    ld_slots, dst, ld_out);
+                                                                                    ld_slots, o, ld_out);
     else
         reduce_slots_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, ranks, rows, cols,
-                                                                                     ld_slots, dst, ld_out);
+                                                                                     ld_slots, o, ld_out);
     return cudaGetLastError() == cudaSuccess ? HGEMM_SM100_OK : HGEMM_SM100_ERR_LAUNCH;
 }
 

@@ -123,6 +123,11 @@ def load() -> ctypes.CDLL:
                                                  ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
                                                  ctypes.c_int64, ctypes.c_void_p]
         lib.hgemm_sm100_reduce_slots.restype = ctypes.c_int
+        lib.hgemm_sm100_reduce_slots_gather.argtypes = [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                                        ctypes.c_int64, ctypes.c_int64,
+                                                        ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32,
+                                                        ctypes.c_int64, ctypes.c_void_p]
+        lib.hgemm_sm100_reduce_slots_gather.restype = ctypes.c_int
         lib.hgemm_sm100_alloc_shared.argtypes = [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]
         lib.hgemm_sm100_alloc_shared.restype = ctypes.c_int
         lib.hgemm_sm100_free_shared.argtypes = [ctypes.c_void_p]
@@ -199,6 +204,23 @@ def reduce_slots(slots_ptr: int, ranks: int, rows: int, cols: int, ld_slots: int
                  stream: int = 0) -> int:
     return load().hgemm_sm100_reduce_slots(slots_ptr, ranks, rows, cols, ld_slots, out_ptr, ld_out,
                                            ctypes.c_void_p(stream))
+
+
+def reduce_slots_gather(slots_ptr: int, ranks: int, rows: int, cols: int, ld_slots: int, out_ptrs: list[int],
+                        ld_out: int, stream: int = 0) -> int:
+    outs = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
+    return load().hgemm_sm100_reduce_slots_gather(slots_ptr, ranks, rows, cols, ld_slots, outs, len(out_ptrs),
+                                                  ld_out, ctypes.c_void_p(stream))
+
+
+class DeviceArray:
+    """A device buffer of this library (e.g. hgemm_sm100_alloc_shared) seen
+    through the CUDA array interface, so that ``torch.as_tensor`` wraps it
+    without a copy. The buffer must outlive the tensor."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 2, "strides": None}
 
 
 def _checked(rc: int, what: str) -> None:

@@ -94,7 +94,10 @@ class RowScatter:
             raise ValueError(f"at most {capi.MAX_RANKS} ranks")
         self.rows_per_rank, self.cols, self.rank, self.world, self.group = rows_per_rank, cols, rank, world, group
         nbytes = world * rows_per_rank * cols * 4
+        # Two slot buffers (alternate steps) and the FP16 [M, cols] output
+        # that the all-gather fills on every rank.
         self.local = [capi.alloc_shared(nbytes) for _ in range(2)]
+        self.local.append(capi.alloc_shared(world * rows_per_rank * cols * 2))
         handles = [capi.ipc_handle(p) for p in self.local]
         gathered = [None] * world
         if world > 1:
@@ -102,8 +105,8 @@ class RowScatter:
         else:
             gathered[0] = handles
         self.opened = []
-        self.dest = []
-        for b in range(2):
+        self.dest = []          # dest[b][q]: slot buffer b of rank q; dest[2][q]: output of rank q
+        for b in range(3):
             row = []
             for q in range(world):
                 if q == rank:
@@ -113,6 +116,9 @@ class RowScatter:
                     self.opened.append(ptr)
                     row.append(ptr)
             self.dest.append(row)
+        device = torch.device("cuda", torch.cuda.current_device())
+        self.output = torch.as_tensor(capi.DeviceArray(self.local[2], (world * rows_per_rank, cols), "<f2"),
+                                      device=device)
         self.steps = 0
 
     def close(self) -> None:
@@ -126,6 +132,7 @@ class RowScatter:
         self.opened = []
         if self.world > 1:
             dist.barrier(group=self.group)     # every peer has unmapped them
+        self.output = None
         for ptr in self.local:
             capi.free_shared(ptr)
         self.local = []
@@ -143,6 +150,7 @@ class TensorParallelMLP:
     gemm: Callable = _cuda_gemm
     gemm_f32: Callable = _cuda_gemm_f32
     inter_total: int | None = None
+    down_mode: str = "all_reduce"     # or "p2p" (fused peer-memory path, CUDA only)
 
     def __post_init__(self):
         m = self.x.shape[0]
@@ -189,9 +197,22 @@ class TensorParallelMLP:
         return self.gemm(self.x, self.w_up, self.y)
 
     def down(self) -> torch.Tensor:
+        """Row-parallel down-projection with the full FP16 output on every
+        rank. ``down_mode`` "all_reduce": FP32 partial, NCCL all-reduce, one
+        rounding; "p2p": the fused peer-memory path (:meth:`down_p2p` with
+        the all-gather), the same value summed in rank order."""
+        if self.down_mode == "p2p":
+            self.out = self.down_p2p(gather=True)
+            return self.out
+        return self.down_all_reduce()
+
+    def down_all_reduce(self) -> torch.Tensor:
+        """FP32 partial, NCCL all-reduce (SUM), one FP16 rounding."""
         self.gemm_f32(self.h, self.w_down, self.partial)
         if self.world > 1:
             dist.all_reduce(self.partial, op=dist.ReduceOp.SUM, group=self.group)
+        if self.out is getattr(getattr(self, "scatter", None), "output", None):
+            self.out = torch.empty_like(self.out)       # leave the p2p output alone
         self.out.copy_(self.partial)          # the single FP16 rounding
         return self.out
 
@@ -235,9 +256,16 @@ class TensorParallelMLP:
         self.shard.copy_(self.shard_f32)      # the single FP16 rounding of the owned rows
         return self.shard
 
-    def down_p2p(self) -> torch.Tensor:
+    def down_p2p(self, gather: bool = False) -> torch.Tensor:
         """Fused GEMM + reduce-scatter over peer memory: returns this rank's
-        FP16 [M / G, hidden] shard (rows [r * M / G, (r + 1) * M / G))."""
+        FP16 [M / G, hidden] shard (rows [r * M / G, (r + 1) * M / G)).
+
+        With ``gather`` every owner also writes its reduced FP16 rows into all
+        peers' output buffers (an all-gather over NVLink) and a second barrier
+        completes them: the result is the full FP16 [M, hidden] output on
+        every rank, the same value an FP32 all-reduce followed by one rounding
+        gives (the slots are added in rank order). Its consumers run on this
+        stream; the next call rewrites it."""
         from . import capi
 
         m, hidden = self.partial.shape
@@ -265,16 +293,28 @@ class TensorParallelMLP:
         if self.world > 1:
             # Orders every rank's GEMM (its peer stores) before any owner reads.
             dist.all_reduce(self._barrier_flag, op=dist.ReduceOp.MAX, group=self.group)
-        rc = capi.reduce_slots(sc.local[buf], self.world, rows, hidden, hidden, self.shard_p2p.data_ptr(), hidden,
-                               stream)
+        if gather:
+            offset = self.rank * rows * hidden * 2          # this rank's rows in every output
+            outs = [sc.dest[2][q] + offset for q in range(self.world)]
+            rc = capi.reduce_slots_gather(sc.local[buf], self.world, rows, hidden, hidden, outs, hidden, stream)
+        else:
+            rc = capi.reduce_slots(sc.local[buf], self.world, rows, hidden, hidden, self.shard_p2p.data_ptr(),
+                                   hidden, stream)
         if rc != capi.OK:
             raise RuntimeError(f"hgemm_sm100_reduce_slots failed: {capi.status_string(rc)}")
         sc.steps += 1
-        return self.shard_p2p
+        if not gather:
+            return self.shard_p2p
+        if self.world > 1:
+            # Every owner's rows have landed in every output.
+            dist.all_reduce(self._barrier_flag, op=dist.ReduceOp.MAX, group=self.group)
+        return sc.output
 
     def close(self) -> None:
         """Releases the peer mappings and receive buffers (collective)."""
         if getattr(self, "scatter", None) is not None:
+            if self.out is self.scatter.output:
+                self.out = self.out.clone()             # stream-ordered before the buffer is freed
             self.scatter.close()
             self.scatter = None
 
