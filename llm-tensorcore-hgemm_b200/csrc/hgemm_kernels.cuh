@@ -1064,15 +1064,25 @@ struct PersistCfg {
     static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
+// `rot` rotates the M-tile order (a bijection on the tiles).
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m,
-                                            int& tm, int& tn) {
+                                            int& tm, int& tn, int rot = 0) {
     const int width = group_m * tiles_n;
     const int g = t / width;
     const int first_m = g * group_m;
     const int gsz = min(tiles_m - first_m, group_m);
     const int in = t - g * width;
     tm = first_m + in % gsz;
+    if (rot != 0) tm = (tm + rot) % tiles_m;
     tn = in / gsz;
+}
+
+// M-tile rotation of a row scatter: rank r starts on the rows of rank r + 1,
+// so that at any time each owner receives from about one peer instead of
+// all of them writing into the same owner's buffer (NVLink incast).
+__device__ __forceinline__ int scatter_rotation(const GemmParams& p, int tile_rows, int tiles_m) {
+    if (p.sc_ranks <= 1) return 0;
+    return static_cast<int>((static_cast<long long>(p.sc_rank + 1) * p.sc_rows / tile_rows) % tiles_m);
 }
 
 template <int kBN, int kStages>
@@ -1124,6 +1134,7 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     const int tiles_m = (p.m + kMmaM - 1) / kMmaM;
+    const int m_rot = scatter_rotation(p, kMmaM, tiles_m);
     const int tiles_n = (p.n + kBN - 1) / kBN;
     const int num_tiles = tiles_m * tiles_n;
     const int nkb = (p.k + kBlockK - 1) / kBlockK;
@@ -1134,7 +1145,7 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int tm, tn;
-                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn, m_rot);
                 for (int kb = 0; kb < nkb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
                     uint8_t* s_a = smem + stage * Cfg::kStageBytes;
@@ -1190,7 +1201,7 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wc))) break;
             tc_fence_after_sync();
             int tm, tn;
-            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn, m_rot);
             const int row = tm * kMmaM + warp * 32 + lane;
             const uint32_t t_acc = tmem_base + t_lane + acc * kBN;
             if (p.tma_store) {
@@ -1326,6 +1337,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
     const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
 
     const int tiles_m = (p.m + Cfg::kTileM - 1) / Cfg::kTileM;
+    const int m_rot = scatter_rotation(p, Cfg::kTileM, tiles_m);
     const int tiles_n = (p.n + Cfg::kTileN - 1) / Cfg::kTileN;
     const int num_tiles = tiles_m * tiles_n;
     const int nkb = (p.k + kBlockK - 1) / kBlockK;
@@ -1338,7 +1350,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             bool ok = true;
             for (int t = pair; t < num_tiles && ok; t += npairs) {
                 int tm, tn;
-                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+                tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn, m_rot);
                 const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kRows;
                 const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
                 for (int kb = 0; kb < nkb; ++kb) {
@@ -1405,7 +1417,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tfull[acc], acc_phase, wc))) break;
             tc_fence_after_sync();
             int tm, tn;
-            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn);
+            tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn, m_rot);
             // Warp w: its 32 TMEM lanes are rows row0 .. row0 + 31 of columns
             // col0 .. col0 + kAccCols - 1 (folded layout: warps 2, 3 hold the
             // right half of the columns of the rows of warps 0, 1).
@@ -1618,6 +1630,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     const int rows_total = kSwap ? p.n : p.m;
     const int cols_total = kSwap ? p.m : p.n;
     const int tiles_r = (rows_total + kMmaM - 1) / kMmaM;
+    const int m_rot = kSwap ? 0 : scatter_rotation(p, kMmaM, tiles_r);
     const int tiles_c = (cols_total + kBNm - 1) / kBNm;
     const int T = tiles_r * tiles_c;
     const int KB = (p.k + kBlockK - 1) / kBlockK;
@@ -1633,7 +1646,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
             Seg sg;
             while (ok && it.next(sg)) {
                 int tr, tc;
-                tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc);
+                tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc, m_rot);
                 const int k_rows0 = kSwap ? tc * kBNm : tr * kMmaM;
                 const int mn_cols0 = kSwap ? tr * kMmaM : tc * kBNm;
                 for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
@@ -1701,7 +1714,7 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
             if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, wc))) break;
             tc_fence_after_sync();
             int tr, tc;
-            tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc);
+            tile_coords(sg.tile, tiles_r, tiles_c, p.group_m, tr, tc, m_rot);
             const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kAccCols;
             const bool produce = sg.kb1 < KB;                 // partial owed to a later CTA
             const bool finish = !produce && sg.kb0 > 0;       // adds earlier CTAs' partials
