@@ -287,6 +287,24 @@ def gpu_reference_check(out, a, b) -> bool:
     return oracle.correctness_passed(oracle.error_metrics(out, ref))
 
 
+POLICY_PATH = Path(__file__).resolve().parent / "llm-tensorcore-hgemm_b200" / "configs" / "sm100_dispatch.json"
+
+
+def load_policy() -> bool:
+    """Loads the committed exact-shape table when it matches this code and
+    GPU (configure_dispatch refuses it otherwise); True when loaded."""
+    from llm_hgemm.dispatch import configure_dispatch
+
+    if not POLICY_PATH.exists():
+        return False
+    try:
+        configure_dispatch(POLICY_PATH, strategy="best_available")
+        return True
+    except ValueError as exc:
+        log(f"policy not used: {exc}")
+        return False
+
+
 def sweep(peaks: dict, quick: bool) -> list[dict]:
     import llm_hgemm
     from llm_hgemm import _comparators
@@ -301,12 +319,19 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
         shapes = [s for s in shapes if s[0] * s[1] * s[2] <= 4096 ** 3]
     peak_t = peaks["bf16_tflops"]
     peak_bw = peaks["hbm_gbs"]
+    policy = load_policy()
     rows = []
     for (m, n, k, tag) in shapes:
         sets = make_sets(m, n, k, "cuda")
         ours = median_launch_us(
             lambda s: _hgemm_out(s[0], s[1], s[2], implementation="auto"), sets)
         lt = median_launch_us(lambda s: _comparators.cublaslt_out(s[0], s[1], s[2]), sets)
+        tuned = None
+        if policy and tag.startswith("qwen3_4b"):
+            # The reference's production path: shape_auto under the committed
+            # exact-shape table (the configuration the tuner measured fastest).
+            tuned = median_launch_us(
+                lambda s: _hgemm_out(s[0], s[1], s[2], implementation="shape_auto"), sets)
         a, b, c = sets[0]
         _hgemm_out(a, b, c, implementation="auto")
         ok = gpu_reference_check(c, a, b)
@@ -330,10 +355,37 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
             "ratio_to_cublaslt": round(lt["median_us"] / t, 3),
             "status": "pass" if ok else "fail",
         })
+        if tuned is not None:
+            sa = sets[0]
+            _hgemm_out(sa[0], sa[1], sa[2], implementation="shape_auto")
+            rows[-1].update({
+                "shape_auto_config": llm_hgemm.dispatch.last_selected(),
+                "shape_auto_us": round(tuned["median_us"], 2),
+                "shape_auto_ratio_to_cublaslt": round(lt["median_us"] / tuned["median_us"], 3),
+                "shape_auto_status": "pass" if gpu_reference_check(sa[2], sa[0], sa[1]) else "fail",
+            })
         log(json.dumps(rows[-1]))
         del sets
         torch.cuda.empty_cache()
     return rows
+
+
+def sweep_summary(rows: list[dict]) -> dict:
+    """Geometric mean of t_cuBLASLt / t_ours over the Qwen3-4B shapes, for
+    `auto` and (when the table is loaded) `shape_auto`."""
+    def geomean(vals):
+        return round(math.exp(sum(math.log(v) for v in vals) / len(vals)), 3) if vals else None
+
+    qwen = [r for r in rows if r["tag"].startswith("qwen3_4b")]
+    out = {"qwen_shapes": len(qwen),
+           "qwen_geomean_ratio_auto": geomean([r["ratio_to_cublaslt"] for r in qwen]),
+           "qwen_shapes_at_or_above_1": sum(r["ratio_to_cublaslt"] >= 1.0 for r in qwen)}
+    tuned = [r["shape_auto_ratio_to_cublaslt"] for r in qwen if "shape_auto_ratio_to_cublaslt" in r]
+    if tuned:
+        out["qwen_geomean_ratio_shape_auto"] = geomean(tuned)
+        out["qwen_best_of_auto_and_shape_auto"] = geomean(
+            [max(r["ratio_to_cublaslt"], r.get("shape_auto_ratio_to_cublaslt", 0.0)) for r in qwen])
+    return out
 
 
 def run_square(args, peaks, peak_kind) -> dict:
@@ -614,6 +666,7 @@ def main() -> None:
         line = run_square(args, peaks, peak_kind)
         if not args.no_sweep:
             line["sweep"] = sweep(peaks, args.quick_sweep)
+            line["sweep_summary"] = sweep_summary(line["sweep"])
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.size, args.size, args.size)
         print(json.dumps(line), flush=True)
