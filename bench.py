@@ -383,8 +383,7 @@ def sweep_summary(rows: list[dict]) -> dict:
     tuned = [r["shape_auto_ratio_to_cublaslt"] for r in qwen if "shape_auto_ratio_to_cublaslt" in r]
     if tuned:
         out["qwen_geomean_ratio_shape_auto"] = geomean(tuned)
-        out["qwen_best_of_auto_and_shape_auto"] = geomean(
-            [max(r["ratio_to_cublaslt"], r.get("shape_auto_ratio_to_cublaslt", 0.0)) for r in qwen])
+        out["qwen_shapes_at_or_above_1_shape_auto"] = sum(v >= 1.0 for v in tuned)
     return out
 
 
