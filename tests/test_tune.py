@@ -88,7 +88,7 @@ def test_selected_policy_loads(tmp_path):
 
 
 def test_shape_sets(tmp_path):
-    assert len(tune.shape_set("qwen3_4b")) == 30
+    assert len(tune.shape_set("qwen3_4b")) == 48
     f = tmp_path / "shapes.json"
     f.write_text(json.dumps([[1, 2, 3]]))
     assert tune.shape_set(str(f)) == [(1, 2, 3)]
