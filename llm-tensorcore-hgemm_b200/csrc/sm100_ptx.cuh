@@ -161,35 +161,6 @@ __device__ __forceinline__ void bulk_wait_group_all() {
     asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-// L2 cache policies for bulk copies (createpolicy): evict_last keeps operand
-// panels resident for the CTAs that reuse them; evict_first lets output lines
-// leave L2 first instead of displacing those panels.
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-__device__ __forceinline__ uint64_t l2_policy_evict_first() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                                 int32_t x, int32_t y, uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%3, %4}], [%2], %5;"
-        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)),
-          "r"(x), "r"(y), "l"(policy)
-        : "memory");
-}
-__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int32_t x, int32_t y,
-                                                  uint64_t policy) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;"
-                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(src)), "r"(x), "r"(y), "l"(policy)
-                 : "memory");
-}
-
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy (tcgen05 / TMA) reads of the same memory.
 __device__ __forceinline__ void fence_async_shared() {
@@ -452,13 +423,6 @@ __device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float a, float b, flo
 }
 __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float a) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(a) : "memory");
-}
-
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-    return v;
 }
 
 // ----------------------------------------------------------- conversions ---
