@@ -2,7 +2,7 @@
 
 Run in the build container, where the reference checkout is mounted:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py <path of the reference checkout>
 
 It loads the reference's own ``llm_hgemm/reference.py`` by file path (a plain
 ``import llm_hgemm`` would need the reference's compiled extension) and, for
@@ -44,7 +44,9 @@ def load_reference(ref_root: Path):
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <path of the reference checkout>")
+    ref_root = Path(sys.argv[1])
     ref = load_reference(ref_root)
     torch.set_num_threads(1)
     arrays = {}
