@@ -84,6 +84,7 @@ struct GemmParams {
     // rank q = i / sc_rows, sc_dest[q] (a peer GPU's memory for q != sc_rank),
     // at row i - q * sc_rows of that slot.
     int sc_ranks, sc_rank, sc_rows;
+    int sc_bulk;               // rows leave through cp.async.bulk (persistent kernel)
     long long sc_ld;
     float* sc_dest[8];
 };
@@ -266,6 +267,28 @@ __device__ __forceinline__ void store_block_f32(const GemmParams& p, float* box,
         if (row < p.m && col < p.n) f32_row(p, row)[col] = box[r * 32 + static_cast<int>(lane ^ static_cast<uint32_t>(r))];
     }
     __syncwarp();
+}
+
+// The same block through the bulk-copy engine: each lane stages its row
+// (128 bytes, row-major) in one of the warp's two 4 KB buffers and hands it to
+// cp.async.bulk (shared -> global; the row's owner may be a peer GPU), so the
+// rows leave the SM as asynchronous bulk transfers rather than LSU stores.
+// A buffer is rewritten only after the copies that read it two blocks ago have
+// read it (each lane commits one bulk group per block). Needs 16-byte-aligned
+// destination rows and n % 4 == 0 (p.sc_bulk).
+__device__ __forceinline__ void store_block_f32_bulk(const GemmParams& p, uint8_t* bufs, uint32_t& buf,
+                                                     uint32_t lane, const uint32_t* v, int row0, int col0) {
+    float* row_buf = reinterpret_cast<float*>(bufs + buf * 4096u) + lane * 32u;
+    bulk_wait_group_read<1>();
+#pragma unroll
+    for (int c = 0; c < 32; c += 4)
+        *reinterpret_cast<uint4*>(row_buf + c) = make_uint4(v[c], v[c + 1], v[c + 2], v[c + 3]);
+    fence_async_shared();
+    const int row = row0 + static_cast<int>(lane);
+    const int cols = min(32, p.n - col0);
+    if (row < p.m && cols > 0) bulk_store(f32_row(p, row) + col0, row_buf, static_cast<uint32_t>(cols) * 4u);
+    bulk_commit_group();
+    buf ^= 1u;
 }
 
 // Swapped tiles: accumulator row = output column `col`, accumulator columns =
@@ -1223,7 +1246,9 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(t_acc + c, v);
                     tmem_wait_ld();
-                    if (p.sc_ranks > 0)
+                    if (p.sc_bulk)
+                        store_block_f32_bulk(p, boxes, buf, lane, v, tm * kMmaM + warp * 32, tn * kBN + c);
+                    else if (p.sc_ranks > 0)
                         store_block_f32(p, reinterpret_cast<float*>(boxes), lane, v, tm * kMmaM + warp * 32, tn * kBN + c);
                     else
                         store_row_segment<32>(p, row, tn * kBN + c, v);
@@ -1233,6 +1258,7 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
             mbar_arrive(&tempty[acc]);
         }
         if (p.tma_store && lane == 0) bulk_wait_group_all();
+        if (p.sc_bulk) bulk_wait_group_all();     // every lane's row copies have landed
     }
 
     __syncwarp();

@@ -775,6 +775,10 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             aligned = aligned && reinterpret_cast<uintptr_t>(sc->dest[q]) % 16 == 0;
         }
         p.vec_ok = aligned;
+        // Bulk row copies: 16-byte-aligned rows (aligned above) of whole 16-byte
+        // pieces; the persistent kernels use them.
+        p.sc_bulk = aligned && a.n % 4 == 0 &&
+                    (cfg == HGEMM_SM100_CFG_PERSISTENT_128x256 || cfg == HGEMM_SM100_CFG_PERSISTENT_128x128);
     }
     p.epi_vec = (p.epi & HGEMM_SM100_EPI_BIAS ? reinterpret_cast<uintptr_t>(a.bias) % 16 == 0 : true) &&
                 (p.epi & HGEMM_SM100_EPI_RESIDUAL
