@@ -5,6 +5,13 @@
 
 Runs `--warmup` untimed launches and `--iters` launches of one implementation
 on seeded inputs (randn*0.1, FP16) and exits; nothing is timed here.
+
+With `--case IMPL:MxNxK` (repeatable) one process runs several shapes in turn,
+each with its own inputs, `--warmup` + `--iters` launches (so one `ncu`
+command captures every shipped configuration):
+
+    python llm-tensorcore-hgemm_b200/profile_one.py --warmup 2 --iters 1 \
+        --case tc_pair_128x128:512x4096x2560 --case tc_splitk_128x256:512x2560x4096
 """
 
 from __future__ import annotations
@@ -22,9 +29,11 @@ from llm_hgemm.ops import _hgemm_out, resolved_config  # noqa: E402
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("--m", type=int, required=True)
-    p.add_argument("--n", type=int, required=True)
-    p.add_argument("--k", type=int, required=True)
+    p.add_argument("--m", type=int)
+    p.add_argument("--n", type=int)
+    p.add_argument("--k", type=int)
+    p.add_argument("--case", action="append", default=[], metavar="IMPL:MxNxK",
+                   help="implementation and shape; repeatable (replaces --m/--n/--k/--implementation)")
     p.add_argument("--implementation", default="auto")
     p.add_argument("--provider", choices=["hgemm", "cublaslt"], default="hgemm",
                    help="cublaslt: the benchmark-only comparator on the same inputs")
@@ -32,23 +41,36 @@ def main() -> None:
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--seed", type=int, default=2026)
     args = p.parse_args()
-    torch.manual_seed(args.seed)
-    a = torch.randn((args.m, args.k), device="cuda", dtype=torch.float16) * 0.1
-    b = torch.randn((args.k, args.n), device="cuda", dtype=torch.float16) * 0.1
-    c = torch.empty((args.m, args.n), device="cuda", dtype=torch.float16)
-    if args.provider == "cublaslt":
+    if args.case:
+        for case in args.case:
+            impl, shape = case.split(":")
+            m, n, k = (int(v) for v in shape.lower().split("x"))
+            run_one(m, n, k, impl, args.provider, args.warmup, args.iters, args.seed)
+        return
+    if args.m is None or args.n is None or args.k is None:
+        p.error("--m, --n and --k are required without --case")
+    run_one(args.m, args.n, args.k, args.implementation, args.provider, args.warmup, args.iters, args.seed)
+
+
+def run_one(m: int, n: int, k: int, implementation: str, provider: str, warmup: int, iters: int,
+            seed: int) -> None:
+    torch.manual_seed(seed)
+    a = torch.randn((m, k), device="cuda", dtype=torch.float16) * 0.1
+    b = torch.randn((k, n), device="cuda", dtype=torch.float16) * 0.1
+    c = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    if provider == "cublaslt":
         from llm_hgemm import _comparators
 
-        for _ in range(args.warmup + args.iters):
+        for _ in range(warmup + iters):
             _comparators.cublaslt_out(a, b, c)
         torch.cuda.synchronize()
-        print(f"profiled {args.m}x{args.n}x{args.k} cublaslt comparator")
+        print(f"profiled {m}x{n}x{k} cublaslt comparator")
         return
-    cfg, split = resolved_config(a, b, args.implementation)
-    for _ in range(args.warmup + args.iters):
-        _hgemm_out(a, b, c, implementation=args.implementation)
+    cfg, split = resolved_config(a, b, implementation)
+    for _ in range(warmup + iters):
+        _hgemm_out(a, b, c, implementation=implementation)
     torch.cuda.synchronize()
-    print(f"profiled {args.m}x{args.n}x{args.k} {args.implementation} -> {cfg} split_k={split}")
+    print(f"profiled {m}x{n}x{k} {implementation} -> {cfg} split_k={split}")
 
 
 if __name__ == "__main__":
