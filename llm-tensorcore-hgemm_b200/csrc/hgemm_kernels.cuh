@@ -16,7 +16,8 @@
 //    fixed order through distributed shared memory (no global workspace).
 //    kSwap computes C^T = B^T A^T so that a few activation rows (decode) sit
 //    on the MMA's N side while 128 weight columns fill the MMA's M side.
-//    kTma = false replaces TMA with predicated element loads by warps 0-3 for
+//    kTma = false replaces TMA with loads by warps 0-3 (aligned 16-byte
+//    vectors shifted into place, elements outside the matrix zero) for
 //    operands whose strides or base addresses TMA cannot describe (the role
 //    the reference gives its v5 scalar fallback, csrc/v6_mma_async.cu:428-437).
 //
@@ -447,34 +448,92 @@ __device__ __forceinline__ void store_box_tma_t(const CUtensorMap* map, uint8_t*
 }
 
 // ------------------------------------------------- generic tile loaders ----
+//
+// Operands TMA cannot describe (a base that is not 16-byte aligned, a pitch
+// that is not a multiple of 8 halves) reach the generic tile kernel with only
+// their element (2-byte) alignment. Its loader threads move 8-element pieces
+// (one 16-byte unit of the swizzled tile): each piece's bytes lie in at most
+// two 16-byte-aligned vectors, which are loaded whole and shifted into place.
+// A vector is loaded only when it holds an element of the operand, so no load
+// reaches outside the 16-byte blocks - and so the pages - that the operand's
+// own elements occupy; elements outside the matrix read as zero.
 
-// K-major tile: rows r0 .. r0 + kRows - 1 of the row-major [rows x K] matrix x,
-// K range k0 .. k0 + 63, zero outside the matrix. 128 cooperating threads.
-template <int kRows>
-__device__ __forceinline__ void load_kmaj_generic(uint8_t* dst, const __half* x, long long ldx,
-                                                  int rows, int kdim, int r0, int k0, int tid) {
-#pragma unroll 4
-    for (int idx = tid; idx < kRows * kBlockK; idx += 128) {
-        const int r = idx >> 6, kk = idx & 63;
-        const int gr = r0 + r, gk = k0 + kk;
-        __half v = __float2half_rn(0.f);
-        if (gr < rows && gk < kdim) v = x[static_cast<long long>(gr) * ldx + gk];
-        *reinterpret_cast<__half*>(dst + swz128(r, kk * 2)) = v;
-    }
+struct Piece8 {
+    uint4 v0, v1;   // the aligned vector holding the first element, and the next one
+    uint32_t off;   // byte offset of the first element inside v0 (even)
+    int nv;         // elements of the piece inside the matrix (<= 0: none)
+};
+
+__device__ __forceinline__ Piece8 fetch_piece8(const __half* x, int nv) {
+    Piece8 r;
+    r.v0 = make_uint4(0u, 0u, 0u, 0u);
+    r.v1 = r.v0;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x);
+    r.off = static_cast<uint32_t>(a & 15u);
+    r.nv = nv;
+    const uint4* v = reinterpret_cast<const uint4*>(a - r.off);
+    if (nv > 0) r.v0 = __ldg(v);
+    // v1 starts at element (16 - off) / 2 of the piece.
+    if (r.off != 0u && nv > static_cast<int>((16u - r.off) >> 1)) r.v1 = __ldg(v + 1);
+    return r;
 }
 
-// MN-major tile: columns c0 .. c0 + kCols - 1 of the row-major [K x cols]
-// matrix y, K range k0 .. k0 + 63, zero outside the matrix.
-template <int kCols>
-__device__ __forceinline__ void load_mnmaj_generic(uint8_t* dst, const __half* y, long long ldy,
-                                                   int kdim, int cols, int c0, int k0, int tid) {
-#pragma unroll 4
-    for (int idx = tid; idx < kCols * kBlockK; idx += 128) {
-        const int kk = idx / kCols, c = idx % kCols;
-        const int gk = k0 + kk, gc = c0 + c;
-        __half v = __float2half_rn(0.f);
-        if (gk < kdim && gc < cols) v = y[static_cast<long long>(gk) * ldy + gc];
-        *reinterpret_cast<__half*>(dst + (c >> 6) * kChunkBytes + swz128(kk, (c & 63) * 2)) = v;
+// The piece's 8 elements as one 16-byte unit (little-endian halves), missing
+// elements zero.
+__device__ __forceinline__ uint4 assemble_piece8(const Piece8& r) {
+    const uint32_t w[8] = {r.v0.x, r.v0.y, r.v0.z, r.v0.w, r.v1.x, r.v1.y, r.v1.z, r.v1.w};
+    const uint32_t q = r.off >> 2;               // first word holding a wanted half
+    const bool odd_half = (r.off & 2u) != 0u;    // it starts in that word's upper half
+    uint32_t s[5];
+#pragma unroll
+    for (int i = 0; i < 5; ++i) s[i] = q == 0 ? w[i] : q == 1 ? w[i + 1] : q == 2 ? w[i + 2] : w[i + 3];
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t v = odd_half ? __funnelshift_r(s[i], s[i + 1], 16) : s[i];
+        const uint32_t keep = (2 * i + 1 < r.nv) ? 0xffffffffu : (2 * i < r.nv) ? 0x0000ffffu : 0u;
+        o[i] = v & keep;
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// One stage of the generic tile kernel, by 128 cooperating threads: the
+// K-major tile (rows r0 .. r0 + kKRows - 1 of A, K range k0 .. k0 + 63) and the
+// MN-major tile (K rows k0 .. k0 + 63 of B, columns c0 .. c0 + kMNCols - 1), in
+// the 128-byte-swizzled layout TMA would write. All of a thread's loads are
+// issued before its shared-memory stores.
+template <int kKRows, int kMNCols>
+__device__ __forceinline__ void load_stage_generic(uint8_t* s_k, uint8_t* s_mn, const GemmParams& p, int r0,
+                                                   int c0, int k0, int tid) {
+    constexpr int kKPieces = kKRows * 8 / 128;          // pieces per thread
+    constexpr int kPerRow = kMNCols / 8;
+    constexpr int kMNPieces = 64 * kPerRow / 128;
+    static_assert(kKRows * 8 % 128 == 0 && 64 * kPerRow % 128 == 0, "whole pieces per thread");
+    Piece8 pk[kKPieces], pm[kMNPieces];
+#pragma unroll
+    for (int j = 0; j < kKPieces; ++j) {
+        const int idx = tid + 128 * j;
+        const int gr = r0 + (idx >> 3), gk = k0 + 8 * (idx & 7);
+        const int nv = gr < p.m ? min(p.k - gk, 8) : 0;
+        pk[j] = fetch_piece8(p.a + static_cast<long long>(gr) * p.lda + gk, nv);
+    }
+#pragma unroll
+    for (int j = 0; j < kMNPieces; ++j) {
+        const int idx = tid + 128 * j;
+        const int gk = k0 + idx / kPerRow, gc = c0 + 8 * (idx % kPerRow);
+        const int nv = gk < p.k ? min(p.n - gc, 8) : 0;
+        pm[j] = fetch_piece8(p.b + static_cast<long long>(gk) * p.ldb + gc, nv);
+    }
+#pragma unroll
+    for (int j = 0; j < kKPieces; ++j) {
+        const int idx = tid + 128 * j;
+        *reinterpret_cast<uint4*>(s_k + swz128(idx >> 3, (idx & 7) * 16)) = assemble_piece8(pk[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kMNPieces; ++j) {
+        const int idx = tid + 128 * j;
+        const int kk = idx / kPerRow, c = 8 * (idx % kPerRow);
+        *reinterpret_cast<uint4*>(s_mn + (c >> 6) * kChunkBytes + swz128(kk, (c & 63) * 2)) = assemble_piece8(pm[j]);
     }
 }
 
@@ -834,8 +893,7 @@ hgemm_tile_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constan
             if (!mbar_wait(&empty[stage], phase ^ 1u, wc)) break;
             uint8_t* s_k = smem + stage * Cfg::kStageBytes;
             uint8_t* s_mn = s_k + Cfg::kKBytes;
-            load_kmaj_generic<Cfg::kKRows>(s_k, p.a, p.lda, p.m, p.k, k_rows0, kb * kBlockK, tid);
-            load_mnmaj_generic<Cfg::kMNCols>(s_mn, p.b, p.ldb, p.k, p.n, mn_cols0, kb * kBlockK, tid);
+            load_stage_generic<Cfg::kKRows, Cfg::kMNCols>(s_k, s_mn, p, k_rows0, mn_cols0, kb * kBlockK, tid);
             fence_async_shared();
             mbar_arrive(&full[stage]);
             if (++stage == kStages) { stage = 0; phase ^= 1u; }

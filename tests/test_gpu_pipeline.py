@@ -230,3 +230,32 @@ def test_staged_offset_views_through_api(offsets):
     assert returned is out
     assert_gate(out, a, b)
     assert torch.all(torch.isnan(sc[:oc])) if oc else True
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (37, 53, 29), (129, 130, 67), (200, 264, 520), (300, 7, 1000)])
+@pytest.mark.parametrize("offsets", [(0, 0, 0), (1, 1, 1), (3, 5, 7)])
+def test_generic_nan_guard_bands(shape, offsets):
+    """The generic (no-TMA) kernel loads the 16-byte-aligned vectors around
+    its operands' elements and shifts them into place: NaN before the first
+    element, in the pitch padding of every row and after the last element
+    must never reach the result, and no element outside C is written."""
+    m, n, k = shape
+    oa, ob, oc = offsets
+    lda, ldb, ldc = k + 3, n + 5, n + 1
+    a_ref, b_ref = seeded_inputs(m, n, k)
+    nan = float("nan")
+    sa = torch.full((oa + m * lda + 64,), nan, device="cuda", dtype=torch.float16)
+    sb = torch.full((ob + k * ldb + 64,), nan, device="cuda", dtype=torch.float16)
+    sc = torch.full((oc + m * ldc + 64,), nan, device="cuda", dtype=torch.float16)
+    a = sa[oa:oa + m * lda].view(m, lda)
+    b = sb[ob:ob + k * ldb].view(k, ldb)
+    c = sc[oc:oc + m * ldc].view(m, ldc)
+    a[:, :k].copy_(a_ref)
+    b[:, :n].copy_(b_ref)
+    args = capi.make_args(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, lda=lda, ldb=ldb, ldc=ldc,
+                          config=capi.CFG_GENERIC_128x128)
+    assert capi.run(args, torch.cuda.current_stream().cuda_stream) == capi.OK
+    torch.cuda.synchronize()
+    assert_gate(c[:, :n].contiguous(), a_ref, b_ref)
+    assert torch.all(torch.isnan(c[:, n:])), "pitch padding of C written"
+    assert torch.all(torch.isnan(sc[:oc])) and torch.all(torch.isnan(sc[oc + m * ldc:]))
