@@ -71,6 +71,8 @@ def run_one(m: int, n: int, k: int, implementation: str, provider: str, warmup: 
         _hgemm_out(a, b, c, implementation=implementation)
     torch.cuda.synchronize()
     print(f"profiled {m}x{n}x{k} {implementation} -> {cfg} split_k={split}")
+    del a, b, c
+    torch.cuda.empty_cache()   # the next case starts from an empty device pool
 
 
 if __name__ == "__main__":
