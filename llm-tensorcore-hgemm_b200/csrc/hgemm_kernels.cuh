@@ -3,7 +3,7 @@
 //
 // They replace the reference's kernel family (csrc/v1..v6 of the reference;
 // its best, mma_async_kernel in csrc/v6_mma_async.cu:226-403, is a two-stage
-// cp.async + mma.sync pipeline). Two kernels cover every shape:
+// cp.async + mma.sync pipeline). Four kernel templates cover every shape:
 //
 //  * hgemm_persistent_kernel: one CTA per SM walks 128 x BN output tiles in
 //    grouped raster order. Warp 4 streams A/B tiles with TMA into a STAGES-deep
@@ -11,9 +11,17 @@
 //    tcgen05.mma into one of two TMEM accumulators, warps 0-3 drain the other
 //    accumulator (tcgen05.ld -> FP16 -> global) while the next tile's MMAs run.
 //
+//  * hgemm_pair_kernel: the same persistent scheme on clusters of two CTAs
+//    whose even CTA issues tcgen05.mma.cta_group::2 over both CTAs' tiles.
+//
+//  * hgemm_streamk_kernel: persistent whole-tile waves, then the remaining
+//    tiles' K blocks cut into equal ranges per CTA, partial tiles combined in
+//    a fixed order through the caller's workspace.
+//
 //  * hgemm_tile_kernel: one output tile per CTA, optionally split over K across
 //    the CTAs of a thread-block cluster whose FP32 partials are summed in a
-//    fixed order through distributed shared memory (no global workspace).
+//    fixed order (through the workspace, or distributed shared memory when
+//    the caller gives none).
 //    kSwap computes C^T = B^T A^T so that a few activation rows (decode) sit
 //    on the MMA's N side while 128 weight columns fill the MMA's M side.
 //    kTma = false replaces TMA with loads by warps 0-3 (aligned 16-byte

@@ -215,9 +215,9 @@ KernelEntry g_persist_128 = HG_PERSIST(128, 6);
 KernelEntry g_splitk_128 = HG_TILE(128, false, true, 6);
 KernelEntry g_splitk_256 = HG_TILE(256, false, true, 4);
 KernelEntry g_generic_128 = HG_TILE(128, false, false, 4);
-// Swap-AB tiles for M <= 128 use at most ~110 KB of shared memory so that two
-// CTAs (of different clusters) share an SM; their TMEM (<= 128 columns
-// each) then fits twice into the 512 columns.
+// Swap-AB tiles (decode and small M): rings of 196-216 KB (4-12 stages by
+// width), one CTA per SM, so that each SM keeps about as many weight bytes in
+// flight as its loads need to stream at full rate.
 KernelEntry g_swap_16 = HG_TILE(16, true, true, 12);
 KernelEntry g_swap_32 = HG_TILE(32, true, true, 10);
 KernelEntry g_swap_64 = HG_TILE(64, true, true, 8);
@@ -227,7 +227,7 @@ KernelEntry g_swap_256 = HG_TILE(256, true, true, 4);
 struct SwapChoice {
     int bnm;
     KernelEntry* k;
-    int per_sm;   // CTAs that fit on one SM
+    int per_sm;   // CTAs that fit on one SM (1 with the rings above)
 };
 SwapChoice swap_of_width(int bnm) {
     switch (bnm) {
