@@ -35,19 +35,31 @@ MAX_LOGIT_REL_L2 = 0.001    # reference benchmarks/bench_integration.py:133
 
 def logits_gate(actual: list[torch.Tensor], expected: list[torch.Tensor],
                 max_abs: float = MAX_LOGIT_ABS, max_rel_l2: float = MAX_LOGIT_REL_L2) -> dict:
-    """Largest max-abs and relative-L2 logit error over the given steps; fails
-    on any non-finite logit (reference bench_integration.py:47-70)."""
-    worst_abs, worst_rel, finite = 0.0, 0.0, True
-    for a, e in zip(actual, expected):
+    """Largest max-abs and relative-L2 logit error over the rollout's steps
+    (reference bench_integration.py:47-70): a missing or empty trace and a
+    shape mismatch are errors, not passes; a non-finite logit on either side
+    fails the gate and reports no error figures."""
+    if not actual or len(actual) != len(expected):
+        raise ValueError("empty or different-length logits traces")
+    steps = []
+    for i, (a, e) in enumerate(zip(actual, expected)):
+        if a.shape != e.shape:
+            raise ValueError(f"step {i}: logits shapes {tuple(a.shape)} and {tuple(e.shape)} differ")
         a32, e32 = a.float(), e.float()
-        finite = finite and bool(torch.isfinite(a32).all())
-        d = a32 - e32
-        worst_abs = max(worst_abs, float(d.abs().max()))
-        worst_rel = max(worst_rel, float(torch.linalg.vector_norm(d) /
-                                         torch.linalg.vector_norm(e32).clamp_min(1e-12)))
+        finite = bool(torch.isfinite(a32).all()) and bool(torch.isfinite(e32).all())
+        err_abs = err_rel = None
+        if finite:
+            d = a32 - e32
+            err_abs = float(d.abs().max())
+            err_rel = float(torch.linalg.vector_norm(d) / torch.linalg.vector_norm(e32).clamp_min(1e-12))
+        steps.append({"step": i, "finite": finite, "max_abs": err_abs, "relative_l2": err_rel})
+    finite = all(s["finite"] for s in steps)
+    worst_abs = max(s["max_abs"] for s in steps) if finite else None
+    worst_rel = max(s["relative_l2"] for s in steps) if finite else None
     ok = finite and worst_abs <= max_abs and worst_rel <= max_rel_l2
     return {"correctness": "pass" if ok else "fail", "logits_finite": finite,
             "logits_max_abs_error": worst_abs, "logits_max_relative_l2_error": worst_rel,
+            "logits_per_step_errors": steps,
             "max_abs_limit": max_abs, "max_relative_l2_limit": max_rel_l2}
 
 

@@ -72,13 +72,3 @@ def test_small_qwen3_fused_projections_match_stock():
     for out, ref in ((out_pre, ref_pre), (out_dec, ref_dec)):
         gate = mc.logits_gate([out], [ref], max_abs=0.05, max_rel_l2=0.01)
         assert gate["correctness"] == "pass", gate
-
-
-def test_logits_gate_rejects_nonfinite_and_large_errors():
-    mc = load_model_check()
-    ref = torch.ones(4, 8)
-    assert mc.logits_gate([ref.clone()], [ref])["correctness"] == "pass"
-    bad = ref.clone()
-    bad[0, 0] = float("nan")
-    assert mc.logits_gate([bad], [ref])["logits_finite"] is False
-    assert mc.logits_gate([ref * 1.004], [ref])["correctness"] == "fail"
