@@ -278,13 +278,21 @@ def median_launch_us(fn_for_set, sets, warmup=20, samples=50, per_sample=10) -> 
             "min_us": graph_us[0], "eager_median_us": statistics.median(eager_us)}
 
 
-def gpu_reference_check(out, a, b) -> bool:
+def gpu_reference_metrics(out, a, b) -> dict:
+    """The oracle's error metrics of ``out`` plus ``passed`` (the gate):
+    against the CPU oracle up to 2048^3, above that against the same FP32
+    product computed on the GPU with TF32 off (reference bench_square.py:193)."""
     from oracle import reference as oracle
 
     if a.shape[0] * b.shape[1] * a.shape[1] <= 2048 ** 3:
-        return oracle.check(out, a, b)["passed"]
-    ref = oracle.torch_reference(a, b)  # GPU FP32 with TF32 off (reference bench_square.py:193)
-    return oracle.correctness_passed(oracle.error_metrics(out, ref))
+        return oracle.check(out, a, b)
+    metrics = oracle.error_metrics(out, oracle.torch_reference(a, b))
+    metrics["passed"] = oracle.correctness_passed(metrics)
+    return metrics
+
+
+def gpu_reference_check(out, a, b) -> bool:
+    return gpu_reference_metrics(out, a, b)["passed"]
 
 
 POLICY_PATH = Path(__file__).resolve().parent / "llm-tensorcore-hgemm_b200" / "configs" / "sm100_dispatch.json"
@@ -334,7 +342,8 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
                 lambda s: _hgemm_out(s[0], s[1], s[2], implementation="shape_auto"), sets)
         a, b, c = sets[0]
         _hgemm_out(a, b, c, implementation="auto")
-        ok = gpu_reference_check(c, a, b)
+        errors = gpu_reference_metrics(c, a, b)
+        ok = errors.pop("passed")
         cfg, split = resolved_config(a, b, "auto")
         flops = 2.0 * m * n * k
         bytes_ = 2.0 * (m * k + k * n + m * n)
@@ -342,7 +351,7 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
         compute_bound = flops / bytes_ > peak_t * 1e12 / (peak_bw * 1e9)
         rows.append({
             "shape": f"{m}x{n}x{k}", "tag": tag, "config": cfg, "split_k": split,
-            "median_us": round(t, 2), "p95_us": round(ours["p95_us"], 2),
+            "median_us": round(t, 2), "p95_us": round(ours["p95_us"], 2), "min_us": round(ours["min_us"], 2),
             "eager_median_us": round(ours["eager_median_us"], 2),
             "tflops": round(flops / t / 1e6, 1),
             "pct_of_peak": round(100.0 * flops / t / 1e6 / peak_t, 1),
@@ -350,10 +359,12 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
             "bound": "tensor" if compute_bound else "hbm",
             "roofline_frac": round((flops / t / 1e6 / peak_t) if compute_bound
                                    else (bytes_ / t / 1e3 / peak_bw), 3),
-            "cublaslt_us": round(lt["median_us"], 2),
+            "cublaslt_us": round(lt["median_us"], 2), "cublaslt_p95_us": round(lt["p95_us"], 2),
+            "cublaslt_min_us": round(lt["min_us"], 2),
             "cublaslt_eager_us": round(lt["eager_median_us"], 2),
             "ratio_to_cublaslt": round(lt["median_us"] / t, 3),
             "status": "pass" if ok else "fail",
+            "errors": errors,
         })
         if tuned is not None:
             sa = sets[0]
@@ -361,6 +372,7 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
             rows[-1].update({
                 "shape_auto_config": llm_hgemm.dispatch.last_selected(),
                 "shape_auto_us": round(tuned["median_us"], 2),
+                "shape_auto_p95_us": round(tuned["p95_us"], 2), "shape_auto_min_us": round(tuned["min_us"], 2),
                 "shape_auto_ratio_to_cublaslt": round(lt["median_us"] / tuned["median_us"], 3),
                 "shape_auto_status": "pass" if gpu_reference_check(sa[2], sa[0], sa[1]) else "fail",
             })
@@ -368,6 +380,105 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
         del sets
         torch.cuda.empty_cache()
     return rows
+
+
+# Per-shape CSV of the sweep: the reference's column set (benchmarks/schemas.py
+# of the reference, kept so that its report and tuning scripts read the file),
+# then this build's roofline columns. The ncu columns stay empty here, as in
+# the reference; the ncu summaries live in profiles/.
+CSV_FIELDS = [
+    "timestamp", "git_sha", "gpu", "sm", "driver", "cuda", "torch",
+    "provider", "selected_implementation", "version", "M", "N", "K", "layout", "input_dtype",
+    "accum_dtype", "output_dtype", "algo_id", "workspace_bytes", "warmup",
+    "samples", "launches_per_sample", "median_us", "p95_us", "min_us",
+    "tflops", "ratio_to_cublaslt", "max_abs_error", "mean_abs_error",
+    "max_rel_error", "relative_l2_error", "nan_count", "inf_count",
+    "registers_per_thread", "smem_per_block", "achieved_occupancy",
+    "dram_pct", "l2_pct", "tensor_pipe_metric", "status",
+    "roofline_fraction", "achieved_hbm_gbps", "bound", "n_gpus", "tp_mode", "tag",
+]
+PROTOCOL = {"warmup": 20, "samples": 50, "launches_per_sample": 10,
+            "timing": "median of 50 samples, each a CUDA-graph replay of 10 launches over input sets "
+                      "larger than L2 (CUDA events on the current stream); eager medians in the JSON"}
+
+
+def _command(*cmd: str) -> str:
+    try:
+        return subprocess.run(cmd, capture_output=True, text=True, timeout=30).stdout.strip() or "unavailable"
+    except (OSError, subprocess.SubprocessError):
+        return "unavailable"
+
+
+def environment() -> dict:
+    """The run's environment for the CSV rows and the manifest."""
+    from llm_hgemm.provenance import code_fingerprint
+
+    dev = torch.cuda.current_device()
+    props = torch.cuda.get_device_properties(dev)
+    return {
+        "timestamp": time.strftime("%Y-%m-%dT%H:%M:%SZ", time.gmtime()),
+        "git_sha": _command("git", "-C", str(REPO), "rev-parse", "HEAD"),
+        "gpu": props.name, "sm": f"{props.major}.{props.minor}",
+        "driver": _command("nvidia-smi", f"--id={dev}", "--query-gpu=driver_version",
+                           "--format=csv,noheader"),
+        "cuda": torch.version.cuda or "unknown", "torch": torch.__version__,
+        "code_fingerprint": code_fingerprint(), "seed": SEED,
+    }
+
+
+def csv_rows(rows: list[dict], env: dict) -> list[dict]:
+    """One CSV row per shape and provider (auto, shape_auto when the table was
+    loaded, the cuBLASLt comparator)."""
+    common = {key: env.get(key, "") for key in ("timestamp", "git_sha", "gpu", "sm", "driver", "cuda", "torch")}
+    common.update(version="sm100", layout="row-major/row-major", input_dtype="fp16", accum_dtype="fp32",
+                  output_dtype="fp16", warmup=PROTOCOL["warmup"], samples=PROTOCOL["samples"],
+                  launches_per_sample=PROTOCOL["launches_per_sample"], n_gpus=1, tp_mode="none")
+    out = []
+    for r in rows:
+        m, n, k = (int(v) for v in r["shape"].split("x"))
+        shape = dict(common, M=m, N=n, K=k, bound=r["bound"], tag=r["tag"])
+        flops, bytes_ = 2.0 * m * n * k, 2.0 * (m * k + k * n + m * n)
+
+        def timing(us):
+            return {"tflops": round(flops / us / 1e6, 1), "achieved_hbm_gbps": round(bytes_ / us / 1e3, 1)}
+
+        out.append(dict(shape, provider="auto", selected_implementation=r["config"], algo_id=-1,
+                        workspace_bytes="", median_us=r["median_us"], p95_us=r["p95_us"],
+                        min_us=r.get("min_us", ""), ratio_to_cublaslt=r["ratio_to_cublaslt"],
+                        roofline_fraction=r["roofline_frac"], status=r["status"],
+                        **timing(r["median_us"]), **r.get("errors", {})))
+        if "shape_auto_us" in r:
+            out.append(dict(shape, provider="shape_auto", selected_implementation=r["shape_auto_config"],
+                            algo_id=-1, workspace_bytes="", median_us=r["shape_auto_us"],
+                            p95_us=r.get("shape_auto_p95_us", ""), min_us=r.get("shape_auto_min_us", ""),
+                            ratio_to_cublaslt=r["shape_auto_ratio_to_cublaslt"], status=r["shape_auto_status"],
+                            **timing(r["shape_auto_us"])))
+        out.append(dict(shape, provider="cublaslt", selected_implementation="cublaslt", algo_id="",
+                        workspace_bytes=32 * 1024 * 1024, median_us=r["cublaslt_us"],
+                        p95_us=r.get("cublaslt_p95_us", ""), min_us=r.get("cublaslt_min_us", ""),
+                        ratio_to_cublaslt=1.0, **timing(r["cublaslt_us"])))
+    for row in out:
+        for key in CSV_FIELDS:
+            row.setdefault(key, "")
+    return out
+
+
+def write_csv(rows: list[dict], path: Path, env: dict, peaks: dict) -> None:
+    """The sweep as CSV (CSV_FIELDS) plus ``<path>.manifest.json`` with the
+    environment, the timing protocol and the roofline denominators."""
+    import csv
+
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    with path.open("w", newline="") as f:
+        writer = csv.DictWriter(f, fieldnames=CSV_FIELDS, extrasaction="ignore")
+        writer.writeheader()
+        writer.writerows(csv_rows(rows, env))
+    manifest = {"environment": env, "benchmark": PROTOCOL,
+                "peaks": {k: peaks.get(k) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")},
+                "contract": {"input_dtype": "fp16", "accumulation_dtype": "fp32", "output_dtype": "fp16",
+                             "layout": "row-major/row-major", "alpha": 1.0, "beta": 0.0, "allow_tf32": False}}
+    path.with_name(path.name + ".manifest.json").write_text(json.dumps(manifest, indent=2) + "\n")
 
 
 def sweep_summary(rows: list[dict]) -> dict:
@@ -686,6 +797,8 @@ def main() -> None:
     parser.add_argument("--no-sweep", action="store_true", help="skip the per-shape sweep")
     parser.add_argument("--quick-sweep", action="store_true", help="sweep shapes <= 4096^3 only")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--csv", type=Path, default=None,
+                        help="also write the sweep as CSV (+ .manifest.json) at this path")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -706,6 +819,8 @@ def main() -> None:
         if not args.no_sweep:
             line["sweep"] = sweep(peaks, args.quick_sweep)
             line["sweep_summary"] = sweep_summary(line["sweep"])
+            if args.csv is not None:
+                write_csv(line["sweep"], args.csv, environment(), peaks)
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.size, args.size, args.size)
         print(json.dumps(line), flush=True)

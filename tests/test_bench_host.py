@@ -80,3 +80,80 @@ def test_sweep_summary_geomeans():
     assert out["qwen_shapes_at_or_above_1"] == 1
     assert out["qwen_geomean_ratio_shape_auto"] == pytest.approx(2 ** 0.5, rel=1e-3)
     assert out["qwen_shapes_at_or_above_1_shape_auto"] == 2
+
+
+def fake_sweep(monkeypatch, policy_loaded=True):
+    """bench.sweep() with the GPU parts replaced: checks how the per-shape rows
+    are assembled (timings, ratios, error metrics, shape_auto columns)."""
+    import torch
+
+    import llm_hgemm.dispatch
+    import llm_hgemm.ops
+
+    tiny = (torch.zeros(2, 2, dtype=torch.float16),) * 3
+    calls = {"n": 0}       # timing calls since the shape's inputs were made
+
+    def fake_sets(m, n, k, device):
+        calls["n"] = 0
+        return [tiny]
+
+    def fake_timing(fn, sets):
+        base = 10.0 + calls["n"]         # auto 10, cuBLASLt 11, shape_auto 12 us
+        calls["n"] += 1
+        return {"median_us": base, "p95_us": base + 1.0, "min_us": base - 1.0, "eager_median_us": base + 2.0}
+
+    monkeypatch.setattr(bench, "make_sets", fake_sets)
+
+    monkeypatch.setattr(bench, "median_launch_us", fake_timing)
+    errors = {"max_abs_error": 1e-3, "mean_abs_error": 1e-4, "max_rel_error": 0.5,
+              "relative_l2_error": 2e-4, "nan_count": 0, "inf_count": 0}
+    monkeypatch.setattr(bench, "gpu_reference_metrics", lambda out, a, b: dict(errors, passed=True))
+    monkeypatch.setattr(bench, "gpu_reference_check", lambda out, a, b: True)
+    monkeypatch.setattr(bench, "load_policy", lambda: policy_loaded)
+    monkeypatch.setattr(llm_hgemm.ops, "_hgemm_out", lambda *a, **k: None)
+    monkeypatch.setattr(llm_hgemm.ops, "resolved_config", lambda a, b, impl: ("tc_persistent_128x256", 1))
+    monkeypatch.setattr(llm_hgemm.dispatch, "last_selected", lambda: "auto")
+    peaks = {"bf16_tflops": 1651.8, "hbm_gbs": 6493.7, "bf16_tflops_sustained": 1372.7}
+    return bench.sweep(peaks, quick=True), peaks
+
+
+def test_sweep_rows_without_gpu(monkeypatch):
+    rows, _ = fake_sweep(monkeypatch)
+    assert rows and all(r["status"] == "pass" for r in rows)
+    r = next(r for r in rows if r["tag"].startswith("qwen3_4b"))
+    # auto timed first, cuBLASLt second, shape_auto third for a Qwen shape.
+    assert (r["median_us"], r["p95_us"], r["min_us"]) == (10.0, 11.0, 9.0)
+    assert (r["cublaslt_us"], r["cublaslt_p95_us"], r["cublaslt_min_us"]) == (11.0, 12.0, 10.0)
+    assert r["ratio_to_cublaslt"] == pytest.approx(1.1)
+    assert r["shape_auto_us"] == 12.0 and r["shape_auto_status"] == "pass"
+    assert r["errors"]["relative_l2_error"] == 2e-4 and "passed" not in r["errors"]
+    squares = [r for r in rows if r["tag"] == "square"]
+    assert [r["shape"] for r in squares] == ["1024x1024x1024", "2048x2048x2048", "4096x4096x4096"]
+    assert all("shape_auto_us" not in r for r in squares)
+
+
+def test_sweep_csv_and_manifest(monkeypatch, tmp_path):
+    import csv
+
+    rows, peaks = fake_sweep(monkeypatch)
+    env = {"timestamp": "2026-01-01T00:00:00Z", "git_sha": "abc", "gpu": "NVIDIA B200", "sm": "10.0",
+           "driver": "580.159", "cuda": "12.8", "torch": "2.11.0", "code_fingerprint": "f" * 64, "seed": 2026}
+    path = tmp_path / "sweep.csv"
+    bench.write_csv(rows, path, env, peaks)
+    with path.open() as f:
+        reader = csv.DictReader(f)
+        assert reader.fieldnames == bench.CSV_FIELDS
+        out = list(reader)
+    qwen = sum(r["tag"].startswith("qwen3_4b") for r in rows)
+    assert len(out) == 2 * len(rows) + qwen          # auto + cuBLASLt, + shape_auto on Qwen shapes
+    auto = [r for r in out if r["provider"] == "auto"]
+    assert all(r["status"] == "pass" and r["relative_l2_error"] == "0.0002" for r in auto)
+    assert {r["provider"] for r in out} == {"auto", "shape_auto", "cublaslt"}
+    first = out[0]
+    m, n, k = int(first["M"]), int(first["N"]), int(first["K"])
+    assert float(first["tflops"]) == pytest.approx(2 * m * n * k / float(first["median_us"]) / 1e6, rel=1e-3)
+    assert first["gpu"] == "NVIDIA B200" and first["layout"] == "row-major/row-major"
+    manifest = json.loads((tmp_path / "sweep.csv.manifest.json").read_text())
+    assert manifest["environment"]["code_fingerprint"] == "f" * 64
+    assert manifest["benchmark"]["launches_per_sample"] == 10
+    assert manifest["peaks"]["bf16_tflops"] == 1651.8
