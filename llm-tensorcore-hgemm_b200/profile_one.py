@@ -42,14 +42,23 @@ def main() -> None:
     p.add_argument("--seed", type=int, default=2026)
     args = p.parse_args()
     if args.case:
-        for case in args.case:
-            impl, shape = case.split(":")
-            m, n, k = (int(v) for v in shape.lower().split("x"))
+        cases = [parse_case(p, case) for case in args.case]   # all checked before any GPU work
+        for impl, m, n, k in cases:
             run_one(m, n, k, impl, args.provider, args.warmup, args.iters, args.seed)
         return
     if args.m is None or args.n is None or args.k is None:
         p.error("--m, --n and --k are required without --case")
     run_one(args.m, args.n, args.k, args.implementation, args.provider, args.warmup, args.iters, args.seed)
+
+
+def parse_case(parser: argparse.ArgumentParser, case: str) -> tuple[str, int, int, int]:
+    """``IMPL:MxNxK`` -> (IMPL, M, N, K); a malformed case is a usage error."""
+    impl, sep, shape = case.partition(":")
+    dims = shape.lower().split("x")
+    if not sep or not impl or len(dims) != 3 or not all(d.isdigit() and int(d) > 0 for d in dims):
+        parser.error(f"--case {case!r}: expected IMPL:MxNxK with positive sizes")
+    m, n, k = (int(d) for d in dims)
+    return impl, m, n, k
 
 
 def run_one(m: int, n: int, k: int, implementation: str, provider: str, warmup: int, iters: int,

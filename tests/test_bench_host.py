@@ -157,3 +157,11 @@ def test_sweep_csv_and_manifest(monkeypatch, tmp_path):
     assert manifest["environment"]["code_fingerprint"] == "f" * 64
     assert manifest["benchmark"]["launches_per_sample"] == 10
     assert manifest["peaks"]["bf16_tflops"] == 1651.8
+
+
+@pytest.mark.parametrize("case", ["auto:64x64", "auto:0x64x64", ":64x64x64"])
+def test_profile_driver_rejects_malformed_cases(case):
+    proc = subprocess.run([sys.executable, str(REPO / "llm-tensorcore-hgemm_b200" / "profile_one.py"),
+                           "--case", "auto:64x64x64", "--case", case], capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 2, proc.stderr[-1000:]
+    assert "expected IMPL:MxNxK" in proc.stderr
