@@ -174,39 +174,72 @@ def device_time_ms(fn, steps: int, warmup: int, stream, barrier=None) -> float:
 
 
 # ------------------------------------------------------------ CPU baseline --
+#
+# One sampling rule for the CPU figures (`cpu_baseline` of this arm and every
+# step of `--impl reference`): the reference's CPU path (its oracle: FP32
+# matmul of the FP16 operands, one FP16 rounding) on rows 0..R-1 of A of every
+# GEMM of the workload's step, full N and K, with all of torch's host threads.
+# R is sized from a 64-row probe so that one sampled step takes about
+# CPU_STEP_S seconds; the figure is the sampled FLOPs over the time.
 
-def cpu_baseline(m: int, n: int, k: int, budget_s: float = 12.0) -> dict:
-    """Oracle FP32 GEMM (reference torch_reference) on host cores over row
-    samples of A; returns TFLOP/s of the sampled work."""
-    from oracle import reference as oracle
+CPU_STEP_S = 1.0
 
-    threads = torch.get_num_threads()
-    g = torch.Generator().manual_seed(SEED)
-    b = (torch.randn((k, n), generator=g) * 0.1).half()
-    rows = min(m, 64)
-    a = (torch.randn((rows, k), generator=g) * 0.1).half()
-    t0 = time.perf_counter()
-    oracle.torch_reference(a, b)
-    first = time.perf_counter() - t0
-    # Grow the row sample to fill about budget_s / 3 per call, 3 calls.
-    target = budget_s / 3.0
-    rows = int(min(m, max(rows, rows * target / max(first, 1e-3))))
-    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+
+def workload_gemms(workload: str, size: int) -> list[tuple[int, int, int]]:
+    """(M, N, K) of the GEMMs of one step of `workload`."""
+    if workload == "tp_mlp":
+        return [(8192, 28672, 8192), (8192, 8192, 28672)]
+    return [(size, size, size)]
+
+
+class CpuSample:
+    """The sampled CPU step of a workload (see the rule above)."""
+
+    def __init__(self, gemms: list[tuple[int, int, int]], step_s: float = CPU_STEP_S):
+        from oracle import reference as oracle
+
+        self.oracle = oracle
+        self.threads = torch.get_num_threads()
+        g = torch.Generator().manual_seed(SEED)
+        self.bs = [(torch.randn((k, n), generator=g) * 0.1).half() for (_, n, k) in gemms]
+        self.gemms = gemms
+        probe_rows = 64
+        self.a_all = [(torch.randn((min(m, probe_rows), k), generator=g) * 0.1).half() for (m, _, k) in gemms]
+        t0 = time.perf_counter()
+        self.run()
+        probe = time.perf_counter() - t0
+        rows = int(probe_rows * step_s / max(probe, 1e-3))
+        self.rows = max(probe_rows, min(min(m for (m, _, _) in gemms), rows))
+        self.a_all = [(torch.randn((self.rows, k), generator=g) * 0.1).half() for (_, _, k) in gemms]
+        self.flops = sum(2.0 * self.rows * n * k for (_, n, k) in gemms)
+
+    def run(self) -> None:
+        for a, b in zip(self.a_all, self.bs):
+            self.oracle.torch_reference(a, b)
+
+    def describe(self) -> str:
+        shapes = " + ".join(f"{m}x{n}x{k}" for (m, n, k) in self.gemms)
+        return (f"A rows 0..{self.rows - 1} of each GEMM of the step ({shapes}; full N, K), "
+                f"reference CPU path (FP32 matmul + FP16 rounding), {self.threads} threads of "
+                f"{os.cpu_count()} CPUs; rows sized for ~{CPU_STEP_S:g} s per sampled step")
+
+
+def cpu_baseline(workload: str, size: int) -> dict:
+    """`cpu_baseline` of this arm: median of 3 sampled CPU steps."""
+    sample = CpuSample(workload_gemms(workload, size))
     times = []
     for _ in range(3):
         t0 = time.perf_counter()
-        oracle.torch_reference(a, b)
+        sample.run()
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     return {
-        "value": round(2.0 * rows * n * k / t / 1e12, 4),
+        "value": round(sample.flops / t / 1e12, 4),
         "unit": UNIT,
-        "cores": threads,
+        "cores": sample.threads,
         "kind": "port",
-        "sample": f"A rows 0..{rows - 1} of the {m}x{n}x{k} problem (full N, K), "
-                  f"median of 3 calls of the oracle (FP32 matmul + FP16 rounding), "
-                  f"{threads} threads of {os.cpu_count()} CPUs",
-        "seconds_per_call": round(t, 3),
+        "sample": sample.describe() + "; median of 3",
+        "seconds_per_step": round(t, 3),
     }
 
 
@@ -495,6 +528,23 @@ def sweep_summary(rows: list[dict]) -> dict:
     if tuned:
         out["qwen_geomean_ratio_shape_auto"] = geomean(tuned)
         out["qwen_shapes_at_or_above_1_shape_auto"] = sum(v >= 1.0 for v in tuned)
+    # Compact per-shape tables (the full rows go to stderr, --csv, --sweep-json):
+    # t_cuBLASLt / t_auto per layer at each M, and for M <= 128 the fraction of
+    # the measured HBM copy bandwidth reached.
+    by_layer, hbm = {}, {}
+    for r in qwen:
+        layer = r["tag"].split(".", 1)[1]
+        by_layer.setdefault(layer, []).append(r["ratio_to_cublaslt"])
+        if int(r["shape"].split("x")[0]) <= 128:
+            hbm.setdefault(layer, []).append(r["roofline_frac"])
+    out["qwen_m"] = [m for m in QWEN_M]
+    out["ratio_by_layer"] = by_layer
+    out["hbm_frac_m_le_128"] = hbm
+    out["square_ratio"] = {r["shape"]: r["ratio_to_cublaslt"] for r in rows if r["tag"] == "square"}
+    out["square_tflops"] = {r["shape"]: r["tflops"] for r in rows if r["tag"] == "square"}
+    out["ragged_ratio"] = {r["shape"]: r["ratio_to_cublaslt"] for r in rows if r["tag"] == "ragged"}
+    out["gate_failures"] = [r["shape"] for r in rows if r["status"] != "pass"]
+    out["shapes"] = len(rows)
     return out
 
 
@@ -747,44 +797,53 @@ def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict
 
 # ------------------------------------------------------ reference CPU arm --
 
-def run_reference_arm(args, workload: tuple[int, int, int], world: int) -> dict:
-    from oracle import reference as oracle
-
-    m, n, k = workload
-    threads = torch.get_num_threads()
-    g = torch.Generator().manual_seed(SEED)
-    b = (torch.randn((k, n), generator=g) * 0.1).half()
-    rows = 64
-    a = (torch.randn((rows, k), generator=g) * 0.1).half()
-    t0 = time.perf_counter()
-    oracle.torch_reference(a, b)
-    probe = time.perf_counter() - t0
-    # Size each step to ~2 s of CPU work, whatever K and W are.
-    rows = int(min(m, max(rows, rows * 2.0 / max(probe, 1e-3))))
-    a = (torch.randn((rows, k), generator=g) * 0.1).half()
+def run_reference_arm(args, workload: str, world: int) -> dict:
+    """The reference's CPU path on this box's host cores, with the sampling
+    rule of `cpu_baseline`: W untimed and K timed sampled steps."""
+    sample = CpuSample(workload_gemms(workload, args.size))
     for _ in range(args.warmup):
-        oracle.torch_reference(a, b)
+        sample.run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.torch_reference(a, b)
+        sample.run()
     dt = (time.perf_counter() - t0) / args.steps
-    value = 2.0 * rows * n * k / dt / 1e12
-    sample = (f"A rows 0..{rows - 1} of {m}x{n}x{k} per step (full N, K), "
-              f"oracle FP32 matmul + FP16 rounding, {threads} threads")
+    value = sample.flops / dt / 1e12
+    name = "tp_mlp" if workload == "tp_mlp" else f"square_{args.size}"
+    config = {"workload": name, "gemms": [f"{m}x{n}x{k}" for (m, n, k) in sample.gemms]}
     return {
         "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+        "higher_is_better": True, "scaling": "strong" if workload == "tp_mlp" else "weak",
+        "vs_baseline": None, "dtype": "fp16",
         "data": f"synthetic: randn*0.1 FP16, seed {SEED}", "impl": "reference",
-        "config": {"workload": f"square_{m}" if world == 1 else "tp_mlp", "M": m, "N": n, "K": k},
-        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+        "config": config,
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": sample.threads, "kind": "port",
+                         "sample": sample.describe()},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
 
 
 # ------------------------------------------------------------------- main --
+
+RESULT_LINE_LIMIT = 4000
+
+
+def compact(line: dict) -> dict:
+    """Keeps the one stdout result line under RESULT_LINE_LIMIT characters (the
+    driver reads the tail of stdout): the sweep's per-shape tables move to
+    stderr first if the line would be longer."""
+    if len(json.dumps(line)) <= RESULT_LINE_LIMIT:
+        return line
+    summary = dict(line.get("sweep_summary", {}))
+    for key in ("square_tflops", "ragged_ratio", "hbm_frac_m_le_128", "ratio_by_layer"):
+        if key in summary:
+            log(json.dumps({key: summary.pop(key)}))
+            line = dict(line, sweep_summary=summary)
+            if len(json.dumps(line)) <= RESULT_LINE_LIMIT:
+                break
+    return line
+
 
 def main() -> None:
     parser = argparse.ArgumentParser(description="HGEMM benchmark (one JSON line)")
@@ -799,31 +858,39 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--csv", type=Path, default=None,
                         help="also write the sweep as CSV (+ .manifest.json) at this path")
+    parser.add_argument("--sweep-json", type=Path, default=None,
+                        help="also write the full sweep rows as JSON at this path")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    # Under torchrun every N (1 included) runs the tensor-parallel MLP, so the
+    # scaling curve compares one workload; a plain `python bench.py` runs the
+    # single-GPU square GEMM and the per-shape sweep.
+    workload = "tp_mlp" if (world > 1 or "LOCAL_RANK" in os.environ) else "square"
 
     if args.impl == "reference":
         if rank != 0:
             return
-        workload = (args.size,) * 3 if world == 1 else (8192, 8192, 28672)
         print(json.dumps(run_reference_arm(args, workload, world)), flush=True)
         return
 
     peaks, peak_kind = load_peaks()
-    if world == 1:
+    if workload == "square":
         line = run_square(args, peaks, peak_kind)
         if not args.no_sweep:
-            line["sweep"] = sweep(peaks, args.quick_sweep)
-            line["sweep_summary"] = sweep_summary(line["sweep"])
+            rows = sweep(peaks, args.quick_sweep)
+            line["sweep_summary"] = sweep_summary(rows)
             if args.csv is not None:
-                write_csv(line["sweep"], args.csv, environment(), peaks)
+                write_csv(rows, args.csv, environment(), peaks)
+            if args.sweep_json is not None:
+                args.sweep_json.parent.mkdir(parents=True, exist_ok=True)
+                args.sweep_json.write_text(json.dumps(rows, indent=1) + "\n")
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.size, args.size, args.size)
-        print(json.dumps(line), flush=True)
+            line["cpu_baseline"] = cpu_baseline("square", args.size)
+        print(json.dumps(compact(line)), flush=True)
         return
 
     import torch.distributed as dist
@@ -835,6 +902,8 @@ def main() -> None:
     try:
         line = run_tp_mlp(args, rank, world, peaks, peak_kind)
         if line is not None:
+            if not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_baseline("tp_mlp", args.size)
             print(json.dumps(line), flush=True)
     finally:
         dist.barrier(device_ids=[local])

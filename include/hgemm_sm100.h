@@ -146,7 +146,8 @@ const char* hgemm_sm100_config_name(int32_t config);
 int32_t hgemm_sm100_num_configs(void);
 
 /* Global-memory workspace a configuration uses for an (m, n, k) problem with
- * aligned operands on the current device: the stream-K configurations' per-CTA
+ * aligned operands on the current device (HGEMM_SM100_CFG_AUTO is resolved to
+ * the configuration it picks first): the stream-K configurations' per-CTA
  * slots and flags, or the split-K tile configurations' partial-tile exchange
  * (at the split the library chooses); 0 otherwise. Counterpart of
  * backend_info()["workspace_bytes"] (reference csrc/dispatch.cpp:104-128). */
@@ -174,16 +175,19 @@ size_t hgemm_sm100_workspace_size(const HgemmSm100Args* args);
  * synchronise the device) on its hot path.
  * - config: HGEMM_SM100_CFG_AUTO (stream-K; swap-AB for m <= 128) or one of
  *   the two stream-K configurations; anything else -> ERR_UNKNOWN_CONFIG.
+ *   With AUTO, a problem whose 128x256 split tail would need more scratch
+ *   than the buffer runs whole tiles on the persistent kernel instead, which
+ *   needs none.
  * - A and B must satisfy the TMA rules (16-byte-aligned bases, lda and ldb
  *   multiples of 8); otherwise ERR_INVALID_ARGUMENT (staging would need
  *   scratch of the operands' size).
- * - A problem whose scratch exceeds the static buffer is rejected with
- *   HGEMM_SM100_ERR_SCRATCH_LIMIT and nothing is launched (the swap-AB
- *   configuration, m <= 128, always fits; a 128x256 stream-K split tail does
- *   not on a 148-SM GPU).
- * - The first call on a device looks up the buffer's device address
- *   (cudaGetSymbolAddress) with that device current; make that first call
- *   before any stream capture.
+ * - An explicit stream-K configuration whose scratch exceeds the static
+ *   buffer is rejected with HGEMM_SM100_ERR_SCRATCH_LIMIT and nothing is
+ *   launched (the swap-AB configuration, m <= 128, always fits; a 128x256
+ *   stream-K split tail does not on a 148-SM GPU).
+ * - The first call of any entry point of this library on a device looks up
+ *   the buffer's device address (cudaGetSymbolAddress) with that device
+ *   current; make that first call before any stream capture.
  * - Every call shares the one buffer and it keeps the last call's contents;
  *   nothing in it needs clearing (each launch's flags carry a fresh value that
  *   stale contents never equal). Calls that overlap on the GPU (for example

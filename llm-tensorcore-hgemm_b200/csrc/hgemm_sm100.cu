@@ -29,6 +29,12 @@ static_assert(sizeof(void*) != 8 || sizeof(HgemmSm100Args) == 152, "HgemmSm100Ar
 
 __device__ int g_status_word;  // status word used when the caller passes none
 
+// Scratch of hgemm_sm100_run_static_scratch, for callers that cannot allocate:
+// a file-scope device array that every GPU loading this library holds until
+// the process exits. In host code the name is only a handle for the symbol,
+// never a device address; device_info() looks its address up once per device.
+static __device__ __align__(256) unsigned char g_static_scratch[HGEMM_SM100_STATIC_SCRATCH_BYTES];
+
 constexpr int kMaxDevices = 64;
 constexpr int kMaxSplit = 16;
 constexpr uint64_t kDefaultTimeoutNs = 2000ull * 1000ull * 1000ull;
@@ -55,6 +61,7 @@ struct DeviceInfo {
     int sms = 0;
     int major = 0, minor = 0;
     int* status_word = nullptr;
+    uint8_t* static_scratch = nullptr;   // device address of g_static_scratch
     int max_cluster = 8;
 };
 
@@ -72,8 +79,13 @@ int device_info(const DeviceInfo** out) {
         err |= cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess;
         err |= cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess;
         if (!err && d.major == 10 && d.minor == 0) {
+            // With `dev` current: the device addresses of the library's own
+            // status word and static scratch on this device.
             err |= cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status_word), g_status_word) !=
                    cudaSuccess;
+            err |= cudaGetSymbolAddress(reinterpret_cast<void**>(&d.static_scratch), g_static_scratch) !=
+                   cudaSuccess;
+            err |= d.status_word == nullptr || d.static_scratch == nullptr;
         }
         g_device_error[dev] = err ? HGEMM_SM100_ERR_CUDA
                                   : ((d.major == 10 && d.minor == 0) ? HGEMM_SM100_OK
@@ -1105,11 +1117,10 @@ extern "C" int32_t hgemm_sm100_num_configs(void) { return HGEMM_SM100_CFG_COUNT;
 
 extern "C" size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t n, int64_t k) {
     if (m <= 0 || n <= 0 || k <= 0 || config < 0 || config >= HGEMM_SM100_CFG_COUNT) return 0;
-    if (!is_streamk(config) && !is_tile_cfg(config)) return 0;
     const DeviceInfo* dev = nullptr;
     if (device_info(&dev) != HGEMM_SM100_OK) return 0;
-    if (is_streamk(config)) return plan_streamk(config, m, n, k, dev->sms).bytes;
-    // The split the tile configuration chooses for aligned operands.
+    // The configuration (auto resolved) and split chosen for aligned operands
+    // when the caller gives every workspace asked for.
     HgemmSm100Args a{};
     static const uint8_t dummy[16] = {};
     a.a = a.b = dummy;
@@ -1122,7 +1133,7 @@ extern "C" size_t hgemm_sm100_workspace_bytes(int32_t config, int64_t m, int64_t
     a.config = config;
     int32_t cfg = 0, split = 0;
     if (resolve_cfg(a, *dev, true, &cfg, &split) != HGEMM_SM100_OK) return 0;
-    return exchange_bytes(cfg, m, n, k, split, dev->sms, dev->max_cluster);
+    return region_need(cfg, split, m, n, k, dev->sms, dev->max_cluster);
 }
 
 extern "C" const char* hgemm_sm100_status_string(int status) {
@@ -1158,32 +1169,10 @@ extern "C" int hgemm_sm100_read_status(int32_t* value, int clear) {
 // ================================================ static-scratch entry point ==
 //
 // For callers that cannot allocate device memory at call time: the stream-K
-// scratch lives in this file-scope device array instead of a caller workspace.
-// In host code `g_static_scratch` only names the symbol (it is not a device
-// address); its device address is looked up once per device below and passed
-// to the kernels like any workspace pointer.
-namespace {
-
-static __device__ __align__(256) unsigned char g_static_scratch[HGEMM_SM100_STATIC_SCRATCH_BYTES];
-
-uint8_t* g_static_scratch_ptr[kMaxDevices];
-int g_static_scratch_rc[kMaxDevices];
-std::once_flag g_static_scratch_once[kMaxDevices];
-
-// Device address of the static scratch on the current device (set up on the
-// first call for that device, with it current).
-int static_scratch(int dev, uint8_t** out) {
-    std::call_once(g_static_scratch_once[dev], [dev] {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-        g_static_scratch_ptr[dev] = static_cast<uint8_t*>(ptr);
-        g_static_scratch_rc[dev] = (e == cudaSuccess && ptr != nullptr) ? HGEMM_SM100_OK : HGEMM_SM100_ERR_CUDA;
-    });
-    *out = g_static_scratch_ptr[dev];
-    return g_static_scratch_rc[dev];
-}
-
-}  // namespace
+// scratch is the file-scope array g_static_scratch (above) instead of a caller
+// workspace; its device address on the current device comes from
+// device_info(), which looks it up on the first call of any entry point on
+// that device.
 
 extern "C" int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* stream_ptr) {
     int rc = check_args(args);
@@ -1196,16 +1185,21 @@ extern "C" int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* 
     if (!fp16_tma_ok(args->a, args->lda) || !fp16_tma_ok(args->b, args->ldb))
         return HGEMM_SM100_ERR_INVALID_ARGUMENT;
 
+    const bool automatic = args->config == HGEMM_SM100_CFG_AUTO;
     int32_t cfg = args->config;
-    if (cfg == HGEMM_SM100_CFG_AUTO)
-        cfg = args->m <= 128 ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_STREAMK_128x256;
+    if (automatic) cfg = args->m <= 128 ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_STREAMK_128x256;
     if (!is_streamk(cfg)) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
     if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB && args->m > 128) cfg = HGEMM_SM100_CFG_STREAMK_128x256;
 
     const StreamKPlan sp = plan_streamk(cfg, args->m, args->n, args->k, dev->sms);
-    if (sp.bytes > HGEMM_SM100_STATIC_SCRATCH_BYTES) return HGEMM_SM100_ERR_SCRATCH_LIMIT;
-    uint8_t* scratch = nullptr;
-    if (sp.bytes > 0 && (rc = static_scratch(devid, &scratch)) != HGEMM_SM100_OK) return rc;
+    if (sp.bytes > HGEMM_SM100_STATIC_SCRATCH_BYTES) {
+        // A split tail that does not fit: `auto` runs whole tiles with the
+        // persistent kernel (no scratch); an explicit stream-K request fails.
+        if (!automatic) return HGEMM_SM100_ERR_SCRATCH_LIMIT;
+        return run_core(*args, HGEMM_SM100_CFG_PERSISTENT_128x256, 1, *dev, devid,
+                        static_cast<cudaStream_t>(stream_ptr), nullptr, 0);
+    }
+    uint8_t* scratch = sp.bytes > 0 ? dev->static_scratch : nullptr;
     return run_core(*args, cfg, 1, *dev, devid, static_cast<cudaStream_t>(stream_ptr), scratch,
                     scratch != nullptr ? HGEMM_SM100_STATIC_SCRATCH_BYTES : 0);
 }

@@ -14,7 +14,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("implementation"), py::arg("epilogue") = "none", py::arg("bias") = py::none(),
           py::arg("residual") = py::none());
     m.def("has_cutlass", &has_cutlass);
-    m.def("backend_info", &backend_info, py::arg("implementation"));
+    m.def("backend_info", &backend_info, py::arg("implementation"), py::arg("m") = 0, py::arg("n") = 0,
+          py::arg("k") = 0);
     m.def("hgemm_out_f32", &hgemm_out_f32, py::arg("a"), py::arg("b"), py::arg("out"),
           py::arg("implementation") = "auto");
     m.def("implementations", &implementations);

@@ -165,10 +165,14 @@ void hgemm_out_f32(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor
 
 bool has_cutlass() { return false; }
 
-std::map<std::string, int64_t> backend_info(const std::string& implementation) {
+std::map<std::string, int64_t> backend_info(const std::string& implementation, int64_t m, int64_t n, int64_t k) {
     const int32_t cfg = config_id(implementation);
-    return {{"algorithm_id", -1},
-            {"workspace_bytes", static_cast<int64_t>(hgemm_sm100_workspace_bytes(cfg, 0, 0, 0))}};
+    // Without a shape (the reference's form) there is no workspace to
+    // report; with one, the bytes an aligned problem of that shape takes on
+    // the current device (stream-K partial slots, split-K exchange slots).
+    const bool shaped = m > 0 && n > 0 && k > 0;
+    const int64_t ws = shaped ? static_cast<int64_t>(hgemm_sm100_workspace_bytes(cfg, m, n, k)) : 0;
+    return {{"algorithm_id", -1}, {"workspace_bytes", ws}};
 }
 
 std::vector<std::string> implementations() {

@@ -42,7 +42,8 @@ void hgemm_out_f32(const torch::Tensor& a, const torch::Tensor& b, torch::Tensor
 bool has_cutlass();
 
 // Reference csrc/dispatch.cpp:104-128.
-std::map<std::string, int64_t> backend_info(const std::string& implementation);
+std::map<std::string, int64_t> backend_info(const std::string& implementation, int64_t m = 0, int64_t n = 0,
+                                            int64_t k = 0);
 
 // Names of the kernel configurations, in C-ABI id order ("auto" first).
 std::vector<std::string> implementations();

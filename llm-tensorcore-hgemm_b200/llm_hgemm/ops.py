@@ -95,13 +95,22 @@ def available_providers() -> tuple[str, ...]:
     return ("torch", "shape_auto", *_C.implementations())
 
 
-def backend_info(implementation: str) -> dict[str, int]:
-    """``{"algorithm_id", "workspace_bytes"}`` (reference ops.py:72-77)."""
+def backend_info(implementation: str, shape: tuple[int, int, int] | None = None) -> dict[str, int]:
+    """``{"algorithm_id", "workspace_bytes"}`` (reference ops.py:72-77).
+
+    ``algorithm_id`` is -1 for every custom kernel, as in the reference. With
+    ``shape=(M, N, K)`` the workspace is the one ``hgemm`` allocates for an
+    aligned problem of that shape on the current device (stream-K partial
+    tiles, split-K exchange slots; ``auto`` resolved first); without a shape,
+    as in the reference's call form, it is 0."""
     if implementation == "torch":
         return {"algorithm_id": -1, "workspace_bytes": 0}
     if implementation == "shape_auto":
         implementation = last_selected()
-    return dict(_C.backend_info(implementation))
+    if shape is None:
+        return dict(_C.backend_info(implementation))
+    m, n, k = (int(v) for v in shape)
+    return dict(_C.backend_info(implementation, m, n, k))
 
 
 def resolved_config(a: torch.Tensor, b: torch.Tensor,

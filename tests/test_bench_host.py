@@ -71,15 +71,50 @@ def test_clock_summary_without_samples():
 
 
 def test_sweep_summary_geomeans():
-    rows = [{"tag": "qwen3_4b:q:1", "ratio_to_cublaslt": 2.0, "shape_auto_ratio_to_cublaslt": 2.0},
-            {"tag": "qwen3_4b:q:8", "ratio_to_cublaslt": 0.5, "shape_auto_ratio_to_cublaslt": 1.0},
-            {"tag": "square", "ratio_to_cublaslt": 0.1}]
+    rows = [{"tag": "qwen3_4b.q_proj", "shape": "1x4096x2560", "ratio_to_cublaslt": 2.0,
+             "shape_auto_ratio_to_cublaslt": 2.0, "roofline_frac": 0.5, "status": "pass"},
+            {"tag": "qwen3_4b.q_proj", "shape": "512x4096x2560", "ratio_to_cublaslt": 0.5,
+             "shape_auto_ratio_to_cublaslt": 1.0, "roofline_frac": 0.3, "status": "pass"},
+            {"tag": "square", "shape": "1024x1024x1024", "ratio_to_cublaslt": 0.1, "tflops": 100.0,
+             "roofline_frac": 0.1, "status": "fail"}]
     out = bench.sweep_summary(rows)
     assert out["qwen_shapes"] == 2
     assert out["qwen_geomean_ratio_auto"] == pytest.approx(1.0)
     assert out["qwen_shapes_at_or_above_1"] == 1
     assert out["qwen_geomean_ratio_shape_auto"] == pytest.approx(2 ** 0.5, rel=1e-3)
     assert out["qwen_shapes_at_or_above_1_shape_auto"] == 2
+    assert out["ratio_by_layer"] == {"q_proj": [2.0, 0.5]}
+    assert out["hbm_frac_m_le_128"] == {"q_proj": [0.5]}
+    assert out["square_ratio"] == {"1024x1024x1024": 0.1}
+    assert out["gate_failures"] == ["1024x1024x1024"]
+
+
+def test_full_sweep_summary_fits_a_short_result_line(monkeypatch):
+    # The driver reads the last stdout line: the summary of the full sweep
+    # (every square, ragged and Qwen shape) must keep that line short.
+    rows = []
+    for m, n, k, tag in ([(s, s, s, "square") for s in bench.SQUARE]
+                         + [(m, n, k, "ragged") for (m, n, k) in bench.RAGGED]
+                         + [(m, n, k, f"qwen3_4b.{layer}") for layer, (k, n) in bench.QWEN_LAYERS.items()
+                            for m in bench.QWEN_M]):
+        rows.append({"tag": tag, "shape": f"{m}x{n}x{k}", "ratio_to_cublaslt": 0.987,
+                     "shape_auto_ratio_to_cublaslt": 0.991, "roofline_frac": 0.812, "tflops": 1234.5,
+                     "status": "pass"})
+    out = bench.sweep_summary(rows)
+    assert out["shapes"] == len(rows) and out["qwen_shapes"] == 48
+    assert len(json.dumps(out)) < 2500
+
+
+def test_reference_arm_under_torchrun_times_the_tp_workload():
+    # Under torchrun, N = 1 included, both arms run the tensor-parallel MLP.
+    proc = run_bench("--impl", "reference", "--steps", "3", "--warmup", "3",
+                     env_extra={"RANK": "0", "WORLD_SIZE": "1", "LOCAL_RANK": "0"})
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["config"]["workload"] == "tp_mlp"
+    assert line["config"]["gemms"] == ["8192x28672x8192", "8192x8192x28672"]
+    assert line["scaling"] == "strong" and line["value"] > 0
+    assert "A rows 0.." in line["cpu_baseline"]["sample"]
 
 
 def fake_sweep(monkeypatch, policy_loaded=True):

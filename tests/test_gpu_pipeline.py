@@ -165,6 +165,30 @@ def test_provider_metadata(impl):
     assert backend_info(impl) == {"algorithm_id": -1, "workspace_bytes": 0}
 
 
+@pytest.mark.parametrize("impl,shape", [
+    ("tc_streamk_128x256", (2048, 2560, 4096)),     # split tail: partial slots + flags
+    ("tc_streamk_swapab", (1, 151936, 2560)),
+    ("tc_splitk_128x256", (256, 2560, 9728)),        # split-K exchange through the workspace
+    ("auto", (2048, 2560, 4096)),
+    ("auto", (1, 151936, 2560)),
+    ("auto", (8192, 8192, 8192)),                    # whole tiles: none
+    ("tc_persistent_128x256", (8192, 8192, 8192)),
+])
+def test_provider_metadata_per_shape(impl, shape):
+    # backend_info with a shape reports the workspace hgemm allocates for an
+    # aligned problem of that shape: the same bytes the C ABI asks for.
+    m, n, k = shape
+    a, b = seeded_inputs(m, n, k)
+    out = torch.empty((m, n), device="cuda", dtype=torch.float16)
+    cfg = capi.CFG_AUTO if impl == "auto" else CONFIG_IDS[impl]
+    args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, config=cfg)
+    info = backend_info(impl, (m, n, k))
+    assert info["algorithm_id"] == -1
+    assert info["workspace_bytes"] == capi.workspace_size(args)
+    if impl.startswith("tc_streamk") or impl == "tc_splitk_128x256":
+        assert info["workspace_bytes"] > 0
+
+
 @pytest.mark.parametrize("config", list(CONFIG_IDS))
 def test_fp32_output(config):
     m, n, k = 100, 264, 1000
