@@ -205,6 +205,7 @@ class CpuSample:
         self.gemms = gemms
         probe_rows = 64
         self.a_all = [(torch.randn((min(m, probe_rows), k), generator=g) * 0.1).half() for (m, _, k) in gemms]
+        self.run()                 # thread pool and allocator warm-up
         t0 = time.perf_counter()
         self.run()
         probe = time.perf_counter() - t0

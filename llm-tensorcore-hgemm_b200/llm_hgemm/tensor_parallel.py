@@ -200,7 +200,14 @@ class TensorParallelMLP:
         """Row-parallel down-projection with the full FP16 output on every
         rank. ``down_mode`` "all_reduce": FP32 partial, NCCL all-reduce, one
         rounding; "p2p": the fused peer-memory path (:meth:`down_p2p` with
-        the all-gather), the same value summed in rank order."""
+        the all-gather), the same value summed in rank order. With one rank
+        the GEMM writes the FP16 output itself."""
+        if self.world == 1:
+            # One rank: nothing to reduce. The GEMM's own epilogue gives the
+            # same value (the FP32 sum of the K blocks, rounded once).
+            if self.out is getattr(getattr(self, "scatter", None), "output", None):
+                self.out = torch.empty_like(self.out)
+            return self.gemm(self.h, self.w_down, self.out)
         if self.down_mode == "p2p":
             self.out = self.down_p2p(gather=True)
             return self.out

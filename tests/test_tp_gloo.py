@@ -131,3 +131,15 @@ def test_tp_mlp_matches_unsharded(world, mode):
 def test_dead_rank_fails_peer_collective():
     results = run_ranks(2, "die")
     assert results.get(0, "").startswith("error"), results
+
+
+def test_single_rank_down_projection_needs_no_reduction():
+    # One rank (torchrun N=1): the down-projection's GEMM writes the FP16
+    # output itself; the value equals the FP32 partial rounded once.
+    m, hidden, inter = 24, 40, 70
+    mlp = TensorParallelMLP.synthetic(0, 1, seed=11, device="cpu", m=m, hidden=hidden, inter=inter,
+                                      gemm=cpu_gemm, gemm_f32=cpu_gemm_f32, down_mode="p2p")
+    mlp.step()
+    ref = (mlp.h.float() @ mlp.w_down.float()).half()
+    assert torch.equal(mlp.out, ref)
+    assert torch.equal(mlp.y, (mlp.x.float() @ mlp.w_up.float()).half())
