@@ -1353,7 +1353,8 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
 // they keep full efficiency at half the M granularity.
 // Both CTAs' loads complete their bytes on the even CTA's "stage full"
 // barrier (armed once with both CTAs' bytes); the MMA thread commits "stage
-// empty" and "accumulator full" to the barriers of both CTAs; one lane per
+// empty" and "accumulator full" to the barriers of both CTAs with one
+// multicast commit each; one lane per
 // epilogue warp of either CTA arrives on the even CTA's "accumulator empty".
 
 template <int kTileMT, int kTileNT, int kStages>
@@ -1482,15 +1483,11 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     for (int kk = 0; kk < kBlockK / 16; ++kk)
                         tc_mma_f16_pair(d, kmaj_desc(s_a, kk), mnmaj_desc(s_b, kk), Cfg::kIdesc,
                                         (kb > 0 || kk > 0) ? 1u : 0u);
-                    const uint32_t e = smem_addr(&empty[stage]);
-                    tc_commit_pair(e);
-                    tc_commit_pair(map_to_rank(e, 1));
+                    tc_commit_pair_both(smem_addr(&empty[stage]));
                     if (++stage == kStages) { stage = 0; phase ^= 1u; }
                 }
                 if (ok) {
-                    const uint32_t f = smem_addr(&tfull[acc]);
-                    tc_commit_pair(f);
-                    tc_commit_pair(map_to_rank(f, 1));
+                    tc_commit_pair_both(smem_addr(&tfull[acc]));
                 }
             }
             if (!ok) {

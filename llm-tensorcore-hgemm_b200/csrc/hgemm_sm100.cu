@@ -633,6 +633,22 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             cfg = tiles < sms      ? HGEMM_SM100_CFG_SPLITK_128x256
                   : spread_tail    ? HGEMM_SM100_CFG_STREAMK_128x256
                                    : HGEMM_SM100_CFG_PERSISTENT_128x256;
+            // CTA pairs on 256 x 256 tiles (FP16 output): each SM streams 32
+            // instead of 48 KB per K block for the same MMA work, which ran
+            // 5-7 % faster per tile than the 1-CTA kernel on every large
+            // shape measured; they win unless their coarser tiles leave a
+            // worse last wave. Times below in 128 x 256 K blocks of one SM;
+            // the stream-K split tail is charged what it cost when timed
+            // against whole-tile waves (about 40 K blocks).
+            if (tiles >= sms && !(a.flags & HGEMM_SM100_FLAG_OUT_F32)) {
+                const int64_t pairs = sms / 2;
+                const int64_t tiles2 = cdiv(a.m, 256) * cdiv(a.n, 256);
+                const double kb = static_cast<double>(nkb);
+                const double t_pair = static_cast<double>(cdiv(tiles2, pairs)) * kb * 0.94;
+                const double t_one = spread_tail ? static_cast<double>(tiles) / sms * kb + 40.0
+                                                 : static_cast<double>(cdiv(tiles, sms)) * kb;
+                if (t_pair <= t_one) cfg = HGEMM_SM100_CFG_PAIR_256x256;
+            }
             // Narrow tiles when they (with their K split) fill the SMs in one
             // wave: the same MMA time per K block, half the partial tile to
             // exchange, or no split at all.

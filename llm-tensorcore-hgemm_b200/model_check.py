@@ -16,6 +16,14 @@ the swapped model against the stock model and both models' device times. The
 gate result is reported whether it passes or not. Unless ``--no-fused``, a
 second copy of the model (same seed) with fused q|k|v and gate|up
 projections (``fuse_projections``) is checked and timed the same way.
+
+Unless ``--no-fp32``, the same seeded weights are also run as an FP32 model
+(every operation in FP32, TF32 off): the logit error of the stock FP16 model
+(cuBLAS) against it is the FP16-propagation floor, and the swapped and fused
+models' errors against it are reported beside it. Two FP16 models whose GEMMs
+round differently drift apart through 36 layers even when each GEMM is within
+its own tolerance; the floor shows how far the stock FP16 model itself sits
+from the FP32 result.
 """
 
 from __future__ import annotations
@@ -109,24 +117,31 @@ def rollout(model, prompt, decode_prompts, decode_next):
     return pre, dec, t_pre, sorted(times)[len(times) // 2]
 
 
-def main() -> None:
-    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("--layers", type=int, default=36)
-    p.add_argument("--hidden", type=int, default=2560)
-    p.add_argument("--intermediate", type=int, default=9728)
-    p.add_argument("--heads", type=int, default=32)
-    p.add_argument("--kv-heads", type=int, default=8)
-    p.add_argument("--head-dim", type=int, default=128)
-    p.add_argument("--vocab", type=int, default=151936)
-    p.add_argument("--prefill-tokens", type=int, default=2048)
-    p.add_argument("--decode-batch", type=int, default=16)
-    p.add_argument("--context", type=int, default=2048)
-    p.add_argument("--seed", type=int, default=2026)
-    p.add_argument("--implementation", default="auto")
-    p.add_argument("--no-fused", action="store_true",
-                   help="skip the fused-projection variant (second model copy)")
-    args = p.parse_args()
+def fp32_rollout(args, prompt, decode_prompts, decode_next):
+    """Rollout of the same seeded model in FP32 (weights upcast exactly from
+    the FP16 init, TF32 off for matmuls and convolutions)."""
+    model = build_model(args).float()
+    saved = (torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        pre, dec, _, _ = rollout(model, prompt, decode_prompts, decode_next)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = saved
+    del model
+    torch.cuda.empty_cache()
+    return pre, dec
 
+
+def errors_vs(actual: torch.Tensor, expected: torch.Tensor) -> dict:
+    """Max-abs and relative-L2 error of one logits tensor against another."""
+    g = logits_gate([actual], [expected])
+    return {"max_abs": g["logits_max_abs_error"], "relative_l2": g["logits_max_relative_l2_error"]}
+
+
+def check(args) -> dict:
+    """Runs the model check described in the module docstring; returns the
+    result dictionary (what ``main`` prints)."""
     from llm_hgemm.integration import FrozenHgemmLinear, HgemmSwiGLU, fuse_projections, swap_linears
 
     model = build_model(args)
@@ -146,6 +161,7 @@ def main() -> None:
     backends = sorted({str(m.last_backend) for m in adapters})
 
     fused_result = None
+    f_pre = f_dec = None
     if not args.no_fused:
         # The same seeded weights, with fused q|k|v and gate|up (silu_mul
         # epilogue) projections; the remaining linears through FrozenHgemmLinear.
@@ -163,8 +179,19 @@ def main() -> None:
             "prefill": {**logits_gate([f_pre], [ref_pre]), "hgemm_ms": round(tf_pre, 3)},
             "decode": {**logits_gate([f_dec], [ref_dec]), "hgemm_ms": round(tf_dec, 3)},
         }
+    del model
+    torch.cuda.empty_cache()
 
-    result = {
+    floor = None
+    if not args.no_fp32:
+        p32, d32 = fp32_rollout(args, prompt, decode_prompts, decode_next)
+        floor = {"reference": "the same seeded weights in FP32 (TF32 off)"}
+        for name, (pre, dec) in (("stock_fp16", (ref_pre, ref_dec)), ("hgemm_fp16", (out_pre, out_dec)),
+                                 ("hgemm_fused_fp16", (f_pre, f_dec))):
+            if pre is not None:
+                floor[name] = {"prefill": errors_vs(pre, p32), "decode": errors_vs(dec, d32)}
+
+    return {
         "model": "Qwen3-4B architecture, random init (std 0.02), FP16",
         "layers": args.layers, "hidden": args.hidden, "vocab": args.vocab,
         "linears_swapped": swapped, "executed_backends": backends,
@@ -175,8 +202,33 @@ def main() -> None:
                    **logits_gate([out_dec], [ref_dec]),
                    "stock_ms": round(t_dec_ref, 3), "hgemm_ms": round(t_dec, 3)},
         "fused_projections": fused_result,
+        "fp32_floor": floor,
     }
-    print(json.dumps(result), flush=True)
+
+
+def parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--layers", type=int, default=36)
+    p.add_argument("--hidden", type=int, default=2560)
+    p.add_argument("--intermediate", type=int, default=9728)
+    p.add_argument("--heads", type=int, default=32)
+    p.add_argument("--kv-heads", type=int, default=8)
+    p.add_argument("--head-dim", type=int, default=128)
+    p.add_argument("--vocab", type=int, default=151936)
+    p.add_argument("--prefill-tokens", type=int, default=2048)
+    p.add_argument("--decode-batch", type=int, default=16)
+    p.add_argument("--context", type=int, default=2048)
+    p.add_argument("--seed", type=int, default=2026)
+    p.add_argument("--implementation", default="auto")
+    p.add_argument("--no-fused", action="store_true",
+                   help="skip the fused-projection variant (second model copy)")
+    p.add_argument("--no-fp32", action="store_true",
+                   help="skip the FP32 model (the FP16-propagation floor)")
+    return p
+
+
+def main() -> None:
+    print(json.dumps(check(parser().parse_args())), flush=True)
 
 
 if __name__ == "__main__":

@@ -112,7 +112,7 @@ TILE_KERNELS = ("tc_swapab", "tc_splitk_128x256")
     ((1, 151936, 2560), ("tc_streamk_swapab",)), ((16, 4096, 2560), ("tc_swapab",)),
     ((2048, 2560, 4096), ("tc_streamk_128x256",)), ((512, 2560, 4096), TILE_KERNELS),
     ((512, 4096, 2560), TILE_KERNELS), ((512, 1024, 2560), TILE_KERNELS),
-    ((200, 2560, 9728), TILE_KERNELS), ((8192, 8192, 1024), ("tc_persistent_128x256",))])
+    ((200, 2560, 9728), TILE_KERNELS), ((8192, 8192, 1024), ("tc_pair_256x256",))])
 def test_auto_picks_streamk_when_tiles_fill_the_sms(shape, expected):
     a, b = seeded_inputs(*shape)
     cfg, _ = resolved_config(a, b, "auto")
