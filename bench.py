@@ -55,6 +55,13 @@ QWEN_LAYERS = {  # (K, N) of the Qwen3-4B linears, weights stored [K, N]
     "gate_proj": (2560, 9728), "down_proj": (9728, 2560), "lm_head": (2560, 151936),
 }
 QWEN_M = (1, 8, 16, 64, 128, 512, 2048, 8192)
+# Shapes outside the tuned Qwen set: the reference's unseen-shape check (M in
+# {2, 8, 16, 64, 256} x q / o / gate / down, its
+# results/raw/v7_unseen_20260929_053349/unseen_comparison.csv) and the M = 4
+# rows of its trace; M = 8, 16 and 64 are already Qwen rows above.
+UNSEEN_LAYERS = ("q_proj", "o_proj", "gate_proj", "down_proj")
+UNSEEN_M = (2, 4, 256)
+UNSEEN_SET_M = (2, 4, 8, 16, 64, 256)
 SQUARE = (1024, 2048, 4096, 8192, 16384)
 RAGGED = ((8193, 8193, 8192), (8199, 8199, 8192), (8255, 8255, 8192), (4096, 4096, 4103),
           (2049, 2049, 2049))
@@ -357,6 +364,10 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
     for layer, (k, n) in QWEN_LAYERS.items():
         for m in QWEN_M:
             shapes.append((m, n, k, f"qwen3_4b.{layer}"))
+    for layer in UNSEEN_LAYERS:
+        k, n = QWEN_LAYERS[layer]
+        for m in UNSEEN_M:
+            shapes.append((m, n, k, f"unseen.{layer}"))
     if quick:
         shapes = [s for s in shapes if s[0] * s[1] * s[2] <= 4096 ** 3]
     peak_t = peaks["bf16_tflops"]
@@ -369,7 +380,7 @@ def sweep(peaks: dict, quick: bool) -> list[dict]:
             lambda s: _hgemm_out(s[0], s[1], s[2], implementation="auto"), sets)
         lt = median_launch_us(lambda s: _comparators.cublaslt_out(s[0], s[1], s[2]), sets)
         tuned = None
-        if policy and tag.startswith("qwen3_4b"):
+        if policy and (tag.startswith("qwen3_4b") or tag.startswith("unseen")):
             # The reference's production path: shape_auto under the committed
             # exact-shape table (the configuration the tuner measured fastest).
             tuned = median_launch_us(
@@ -544,6 +555,18 @@ def sweep_summary(rows: list[dict]) -> dict:
     out["square_ratio"] = {r["shape"]: r["ratio_to_cublaslt"] for r in rows if r["tag"] == "square"}
     out["square_tflops"] = {r["shape"]: r["tflops"] for r in rows if r["tag"] == "square"}
     out["ragged_ratio"] = {r["shape"]: r["ratio_to_cublaslt"] for r in rows if r["tag"] == "ragged"}
+    # The unseen-shape set: the unseen rows plus the Qwen rows of the same
+    # linears at M = 8, 16, 64.
+    unseen = [r for r in rows if r["tag"].startswith("unseen")] + [
+        r for r in qwen if r["tag"].split(".", 1)[1] in UNSEEN_LAYERS
+        and int(r["shape"].split("x")[0]) in UNSEEN_SET_M]
+    if unseen:
+        out["unseen_shapes"] = len(unseen)
+        out["unseen_geomean_ratio_auto"] = geomean([r["ratio_to_cublaslt"] for r in unseen])
+        out["unseen_at_or_above_1"] = sum(r["ratio_to_cublaslt"] >= 1.0 for r in unseen)
+        tuned_u = [r["shape_auto_ratio_to_cublaslt"] for r in unseen if "shape_auto_ratio_to_cublaslt" in r]
+        if tuned_u:
+            out["unseen_geomean_ratio_shape_auto"] = geomean(tuned_u)
     out["gate_failures"] = [r["shape"] for r in rows if r["status"] != "pass"]
     out["shapes"] = len(rows)
     return out

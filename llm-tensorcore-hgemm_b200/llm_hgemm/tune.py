@@ -47,10 +47,21 @@ def variation(values: list[float]) -> float:
     return (max(values) - min(values)) / med if med > 0 else math.inf
 
 
+# Shapes the table was not tuned on: the reference's unseen-shape validation
+# (M in {2, 8, 16, 64, 256} x the q, o, gate/up and down linears,
+# results/raw/v7_unseen_20260929_053349/unseen_comparison.csv:2-21 of the
+# reference) and the M = 4 rows of its Qwen3-4B trace (configs/qwen3_shapes.csv).
+UNSEEN_LAYERS = {"q_proj": (2560, 4096), "o_proj": (4096, 2560), "gate_proj": (2560, 9728),
+                 "down_proj": (9728, 2560)}
+UNSEEN_M = (2, 4, 8, 16, 64, 256)
+
+
 def shape_set(name: str) -> list[tuple[int, int, int]]:
     """Named shape sets, or a JSON file holding [[M, N, K], ...]."""
     if name == "qwen3_4b":
         return [(m, n, k) for (k, n) in QWEN3_4B_LAYERS.values() for m in QWEN3_4B_M]
+    if name == "unseen":
+        return [(m, n, k) for (k, n) in UNSEEN_LAYERS.values() for m in UNSEEN_M]
     if name == "square":
         return [(s, s, s) for s in (1024, 2048, 4096, 8192)]
     return [tuple(int(v) for v in item) for item in json.loads(Path(name).read_text())]
@@ -205,11 +216,12 @@ def policy_payload(entries: list[dict], environment: dict, *, min_gain: float, m
 # -------------------------------------------------------------- validation --
 
 def validate(dispatch: Path, runs: int = 3, samples: int = 20, seed: int = 7,
-             strategy: str = "best_available") -> dict:
+             strategy: str = "best_available", extra_shapes=None) -> dict:
     """Re-measures ``shape_auto`` under the table (``best_available``: what
     ``configure_dispatch`` loads by default) against the cuBLASLt comparator
     on every policy shape, with input seeds the tuner does not use, and checks
-    each dispatch hit its policy entry. (The reference validates its custom
+    each dispatch hit its policy entry; with ``extra_shapes``, also the shapes
+    the table holds no entry for (:func:`validate_unseen`). (The reference validates its custom
     kernels alone, ``best_custom``, because its baseline is cuBLASLt; here the
     baseline ``auto`` is this library's own kernels too.)"""
     from .dispatch import configure_dispatch, selected_implementation
@@ -244,10 +256,62 @@ def validate(dispatch: Path, runs: int = 3, samples: int = 20, seed: int = 7,
                         "custom_variation": variation(custom), "baseline_variation": variation(base),
                         "stable": shape_stable})
     configure_dispatch(None)
-    return {"dispatch_sha256": file_sha256(dispatch), "strategy": strategy, "environment": payload["environment"],
-            "shape_count": len(shapes),
-            "custom_geomean_percent_of_cublaslt": 100.0 * math.exp(statistics.mean(math.log(r) for r in ratios)),
-            "validation_stability_passed": stable, "details": details}
+    summary = {"dispatch_sha256": file_sha256(dispatch), "strategy": strategy,
+               "environment": payload["environment"], "shape_count": len(shapes),
+               "custom_geomean_percent_of_cublaslt": 100.0 * math.exp(statistics.mean(math.log(r) for r in ratios)),
+               "validation_stability_passed": stable, "details": details}
+    if extra_shapes:
+        summary["unseen"] = validate_unseen(dispatch, extra_shapes, runs=runs, samples=samples, seed=seed,
+                                            strategy=strategy)
+    return summary
+
+
+def validate_unseen(dispatch: Path, shapes, runs: int = 3, samples: int = 20, seed: int = 7,
+                    strategy: str = "best_available") -> dict:
+    """Shapes the table holds no entry for (the reference's unseen-shape
+    check): ``shape_auto`` under the table, ``auto`` and the cuBLASLt
+    comparator, timed as in :func:`validate`, and each result of
+    ``shape_auto`` gated with the reference's limits against its FP32 product
+    (``llm_hgemm.reference``, the reference's report gate) on seeded inputs."""
+    import torch
+
+    from . import reference
+    from .dispatch import configure_dispatch, selected_implementation
+    from .ops import hgemm
+
+    configure_dispatch(dispatch, strategy=strategy)
+    try:
+        payload = measure(shapes, ["shape_auto", "auto", "cublaslt"], runs=runs, samples=samples, seed=seed + 2000)
+        times = {(r["M"], r["N"], r["K"], r["provider"]): r["us"] for r in payload["results"]}
+        details = []
+        for (m, n, k) in shapes:
+            g = torch.Generator(device="cuda").manual_seed(seed + m + n + k)
+            a = (torch.randn((m, k), generator=g, device="cuda", dtype=torch.float32) * 0.1).half()
+            b = (torch.randn((k, n), generator=g, device="cuda", dtype=torch.float32) * 0.1).half()
+            chosen = selected_implementation(a, b, "shape_auto")
+            metrics = reference.error_metrics(hgemm(a, b, implementation="shape_auto"),
+                                              reference.torch_reference(a, b))
+            lt = statistics.median(times[(m, n, k, "cublaslt")])
+            details.append({"M": m, "N": n, "K": k, "implementation": chosen,
+                            "shape_auto_median_us": statistics.median(times[(m, n, k, "shape_auto")]),
+                            "auto_median_us": statistics.median(times[(m, n, k, "auto")]),
+                            "cublaslt_median_us": lt,
+                            "shape_auto_ratio_to_cublaslt": lt / statistics.median(times[(m, n, k, "shape_auto")]),
+                            "auto_ratio_to_cublaslt": lt / statistics.median(times[(m, n, k, "auto")]),
+                            "gate_passed": bool(reference.correctness_passed(metrics)),
+                            "max_abs_error": metrics["max_abs_error"],
+                            "relative_l2_error": metrics["relative_l2_error"]})
+    finally:
+        configure_dispatch(None)
+
+    def geo(key):
+        return 100.0 * math.exp(statistics.mean(math.log(d[key]) for d in details))
+
+    return {"shape_count": len(details),
+            "shape_auto_geomean_percent_of_cublaslt": geo("shape_auto_ratio_to_cublaslt"),
+            "auto_geomean_percent_of_cublaslt": geo("auto_ratio_to_cublaslt"),
+            "at_or_above_cublaslt": sum(d["shape_auto_ratio_to_cublaslt"] >= 1.0 for d in details),
+            "all_gates_passed": all(d["gate_passed"] for d in details), "details": details}
 
 
 # --------------------------------------------------------------------- CLI --
@@ -271,6 +335,8 @@ def main(argv=None) -> None:
     pv.add_argument("--runs", type=int, default=3)
     pv.add_argument("--strategy", default="best_available", choices=("best_available", "best_custom"))
     pv.add_argument("--output", type=Path, required=True)
+    pv.add_argument("--unseen", default=None,
+                    help="also validate a shape set the table was not tuned on (e.g. 'unseen')")
     args = p.parse_args(argv)
 
     if args.cmd == "measure":
@@ -289,11 +355,18 @@ def main(argv=None) -> None:
         print(json.dumps({"entries": len(entries),
                           "custom_over_baseline": sum(e["best_available"] != BASELINE for e in entries)}))
     else:
-        summary = validate(args.dispatch, runs=args.runs, strategy=args.strategy)
+        extra = None
+        if args.unseen:
+            tuned = {(e["M"], e["N"], e["K"]) for e in json.loads(args.dispatch.read_text())["entries"]}
+            extra = [s for s in shape_set(args.unseen) if s not in tuned]
+        summary = validate(args.dispatch, runs=args.runs, strategy=args.strategy, extra_shapes=extra)
         args.output.parent.mkdir(parents=True, exist_ok=True)
         args.output.write_text(json.dumps(summary, indent=2))
-        print(json.dumps({k: summary[k] for k in ("shape_count", "custom_geomean_percent_of_cublaslt",
-                                                  "validation_stability_passed")}))
+        brief = {k: summary[k] for k in ("shape_count", "custom_geomean_percent_of_cublaslt",
+                                         "validation_stability_passed")}
+        if "unseen" in summary:
+            brief["unseen"] = {k: v for k, v in summary["unseen"].items() if k != "details"}
+        print(json.dumps(brief))
 
 
 if __name__ == "__main__":

@@ -96,12 +96,15 @@ def test_full_sweep_summary_fits_a_short_result_line(monkeypatch):
     for m, n, k, tag in ([(s, s, s, "square") for s in bench.SQUARE]
                          + [(m, n, k, "ragged") for (m, n, k) in bench.RAGGED]
                          + [(m, n, k, f"qwen3_4b.{layer}") for layer, (k, n) in bench.QWEN_LAYERS.items()
-                            for m in bench.QWEN_M]):
+                            for m in bench.QWEN_M]
+                         + [(m, *bench.QWEN_LAYERS[layer][::-1], f"unseen.{layer}") for layer in bench.UNSEEN_LAYERS
+                            for m in bench.UNSEEN_M]):
         rows.append({"tag": tag, "shape": f"{m}x{n}x{k}", "ratio_to_cublaslt": 0.987,
                      "shape_auto_ratio_to_cublaslt": 0.991, "roofline_frac": 0.812, "tflops": 1234.5,
                      "status": "pass"})
     out = bench.sweep_summary(rows)
     assert out["shapes"] == len(rows) and out["qwen_shapes"] == 48
+    assert out["unseen_shapes"] == 24       # 12 unseen rows + the Qwen rows at M = 8, 16, 64
     assert len(json.dumps(out)) < 2500
 
 
@@ -179,8 +182,8 @@ def test_sweep_csv_and_manifest(monkeypatch, tmp_path):
         reader = csv.DictReader(f)
         assert reader.fieldnames == bench.CSV_FIELDS
         out = list(reader)
-    qwen = sum(r["tag"].startswith("qwen3_4b") for r in rows)
-    assert len(out) == 2 * len(rows) + qwen          # auto + cuBLASLt, + shape_auto on Qwen shapes
+    tuned = sum(r["tag"].startswith(("qwen3_4b", "unseen")) for r in rows)
+    assert len(out) == 2 * len(rows) + tuned         # auto + cuBLASLt, + shape_auto on Qwen / unseen shapes
     auto = [r for r in out if r["provider"] == "auto"]
     assert all(r["status"] == "pass" and r["relative_l2_error"] == "0.0002" for r in auto)
     assert {r["provider"] for r in out} == {"auto", "shape_auto", "cublaslt"}

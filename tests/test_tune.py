@@ -92,3 +92,16 @@ def test_shape_sets(tmp_path):
     f = tmp_path / "shapes.json"
     f.write_text(json.dumps([[1, 2, 3]]))
     assert tune.shape_set(str(f)) == [(1, 2, 3)]
+
+
+def test_unseen_shape_set_is_the_reference_unseen_check_plus_trace_m4():
+    from llm_hgemm.tune import shape_set
+
+    shapes = shape_set("unseen")
+    assert len(shapes) == 24 and len(set(shapes)) == 24
+    # The reference's 20 unseen shapes (M in {2, 8, 16, 64, 256} x four linears)...
+    for m in (2, 8, 16, 64, 256):
+        for (n, k) in ((2560, 4096), (2560, 9728), (4096, 2560), (9728, 2560)):
+            assert (m, n, k) in shapes
+    # ...and the M = 4 rows of its Qwen3-4B trace.
+    assert {(4, 4096, 2560), (4, 2560, 4096), (4, 9728, 2560), (4, 2560, 9728)} <= set(shapes)
