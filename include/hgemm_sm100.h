@@ -44,8 +44,10 @@ enum {
     HGEMM_SM100_ERR_PIPELINE_TIMEOUT = 5,  /* a kernel wait ran out (status word)*/
     HGEMM_SM100_ERR_TENSOR_MAP = 6,        /* cuTensorMapEncodeTiled failed     */
     HGEMM_SM100_ERR_CUDA = 7,              /* other CUDA runtime error          */
-    HGEMM_SM100_ERR_SCRATCH_LIMIT = 8      /* needs more scratch than the static
+    HGEMM_SM100_ERR_SCRATCH_LIMIT = 8,     /* needs more scratch than the static
                                               buffer of hgemm_sm100_run_static_scratch */
+    HGEMM_SM100_ERR_DEBUG_BOUNDS = 9       /* debug build: a device bounds check
+                                              failed (status word)               */
 };
 
 /* Kernel configurations. Every name is also accepted by
@@ -259,6 +261,34 @@ const char* hgemm_sm100_status_string(int status);
 /* Reads (and with clear != 0 resets) the library's own device status word of
  * the current device. Synchronises the device; for tests and debugging. */
 int hgemm_sm100_read_status(int32_t* value, int clear);
+
+/* ------------------------------------------------------------ debug build --
+ * The same library compiled with -DHGEMM_DEBUG (libhgemm_sm100_debug.so,
+ * `python build.py --debug`) checks, before every global access whose address
+ * the kernels compute themselves (the generic no-TMA tile loader, the operand
+ * staging copy, the epilogue's register stores), that it stays inside its
+ * matrix. A failed check skips the access, records the first failure and sets
+ * HGEMM_SM100_ERR_DEBUG_BOUNDS in the status word; nothing traps. Counterpart
+ * of the debug switch the survey of the reference asks for (the reference has
+ * none: its kernels are checked by sanitizer runs only).
+ *
+ * hgemm_sm100_debug_build: 1 in a debug build, else 0.
+ * hgemm_sm100_debug_read: the first recorded failure of the current device
+ * (source line, or 0 when none, and two indices of the access: row and
+ * column); synchronises the device; clear != 0 resets the record. In a
+ * release build it reports line 0.
+ * hgemm_sm100_debug_vec_touches / _span_in: the checks themselves, on the
+ * host, for tests. A row-major matrix of rows x cols elements of esize bytes,
+ * pitch ld elements, at address base: vec_touches is 1 when the 16-byte-aligned
+ * vector at `vec` holds at least one of its elements (the generic loader's
+ * rule), span_in is 1 when the `count` consecutive elements at `ptr` are
+ * elements of one of its rows. */
+int hgemm_sm100_debug_build(void);
+int hgemm_sm100_debug_read(int32_t* line, int64_t* index0, int64_t* index1, int clear);
+int hgemm_sm100_debug_vec_touches(uint64_t vec, uint64_t base, int64_t rows, int64_t cols, int64_t ld,
+                                  int32_t esize);
+int hgemm_sm100_debug_span_in(uint64_t ptr, int64_t count, uint64_t base, int64_t rows, int64_t cols,
+                              int64_t ld, int32_t esize);
 
 #ifdef __cplusplus
 }

@@ -5,6 +5,8 @@ Produces, next to the Python sources in ``llm_hgemm/``:
 * ``libhgemm_sm100.so`` - the hand-written tcgen05/TMA kernels and the C ABI of
   ``include/hgemm_sm100.h`` (nvcc, ``-gencode arch=compute_100a,code=sm_100a``,
   static CUDA runtime, no torch);
+* ``libhgemm_sm100_debug.so`` - the same with ``-DHGEMM_DEBUG`` (device-side
+  bounds checks that record a failure instead of trapping), for tests;
 * ``_C<EXT_SUFFIX>`` - the pybind11/torch host module (contract checks, name
   dispatch, current-stream launch) linked against ``libhgemm_sm100.so``;
 * ``_comparators<EXT_SUFFIX>`` - benchmark-only cuBLASLt comparator (never in
@@ -40,8 +42,11 @@ CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
 NVCC = str(CUDA_HOME / "bin" / "nvcc")
 
 KERNEL_LIB = OUT_DIR / "libhgemm_sm100.so"
+# The same sources with -DHGEMM_DEBUG: device-side bounds checks that record
+# a failure instead of trapping (include/hgemm_sm100.h, debug build).
+DEBUG_LIB = OUT_DIR / "libhgemm_sm100_debug.so"
 KERNEL_SOURCES = [CSRC / "hgemm_sm100.cu"]
-KERNEL_DEPS = KERNEL_SOURCES + [CSRC / "hgemm_kernels.cuh", CSRC / "sm100_ptx.cuh",
+KERNEL_DEPS = KERNEL_SOURCES + [CSRC / "hgemm_kernels.cuh", CSRC / "sm100_ptx.cuh", CSRC / "debug_checks.cuh",
                                 INCLUDE / "hgemm_sm100.h"]
 HOST_SOURCES = [CSRC / "host" / "bindings.cpp", CSRC / "host" / "contract.cpp",
                 CSRC / "host" / "dispatch.cpp"]
@@ -75,16 +80,18 @@ def _run(cmd: list[str]) -> None:
         raise RuntimeError(f"build step failed: {cmd[0]} ... {cmd[-1]}")
 
 
-def build_kernel_lib(force: bool = False) -> Path:
-    if not force and not _stale(KERNEL_LIB, KERNEL_DEPS):
-        return KERNEL_LIB
+def build_kernel_lib(force: bool = False, debug: bool = False) -> Path:
+    target = DEBUG_LIB if debug else KERNEL_LIB
+    if not force and not _stale(target, KERNEL_DEPS):
+        return target
     BUILD_DIR.mkdir(exist_ok=True)
     cmd = [NVCC, *ARCH_FLAGS, "-O3", "-std=c++17", "-lineinfo", "-Xptxas", "-v",
            "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
+           *(["-DHGEMM_DEBUG"] if debug else []),
            f"-I{INCLUDE}", f"-I{CSRC}", *map(str, KERNEL_SOURCES),
-           "-o", str(KERNEL_LIB)]
+           "-o", str(target)]
     _run(cmd)
-    return KERNEL_LIB
+    return target
 
 
 def _torch_flags() -> tuple[list[str], list[str]]:
@@ -138,10 +145,15 @@ def build_comparator_module(force: bool = False) -> Path | None:
     return target
 
 
-def build(force: bool = False) -> None:
+def build(force: bool = False, debug: bool = True) -> None:
     if shutil.which(NVCC) is None and not Path(NVCC).exists():
         raise RuntimeError(f"nvcc not found at {NVCC}")
-    build_kernel_lib(force)
+    with ThreadPoolExecutor(max_workers=2) as pool:
+        jobs = [pool.submit(build_kernel_lib, force)]
+        if debug:
+            jobs.append(pool.submit(build_kernel_lib, force, True))
+        for j in jobs:
+            j.result()
     build_host_module(force)
     build_comparator_module(force)
 
@@ -149,9 +161,10 @@ def build(force: bool = False) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--force", action="store_true", help="rebuild everything")
+    parser.add_argument("--no-debug", action="store_true", help="skip the -DHGEMM_DEBUG kernel library")
     args = parser.parse_args()
-    build(args.force)
-    print(f"built {KERNEL_LIB.name}, {host_module().name}")
+    build(args.force, debug=not args.no_debug)
+    print(f"built {KERNEL_LIB.name}, {'' if args.no_debug else DEBUG_LIB.name + ', '}{host_module().name}")
 
 
 if __name__ == "__main__":

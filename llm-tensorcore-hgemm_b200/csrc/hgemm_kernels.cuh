@@ -39,6 +39,7 @@
 // in-flight copies and MMAs are drained (also bounded) and TMEM is freed.
 #pragma once
 
+#include "debug_checks.cuh"
 #include "sm100_ptx.cuh"
 
 namespace hgemm {
@@ -103,6 +104,21 @@ struct GemmParams {
 constexpr int kEpiBias = 1;
 constexpr int kEpiResidual = 2;
 constexpr int kEpiSiluMul = 4;
+
+// Debug builds: the `count` consecutive output elements at `ptr` (output
+// row `row`, column `col`) lie inside C. Scatter destinations (peer buffers)
+// are not checked. Release builds: always true.
+__device__ __forceinline__ bool c_span_ok(const GemmParams& p, const void* ptr, long long count, int row, int col) {
+#ifdef HGEMM_DEBUG
+    if (p.sc_ranks > 0) return true;
+    const Extent x{reinterpret_cast<uintptr_t>(p.c), p.m, (p.epi & kEpiSiluMul) ? p.n / 2 : p.n, p.ldc,
+                   p.out_f32 ? 4 : 2};
+    return HG_DEBUG_OK(span_in_matrix(reinterpret_cast<uintptr_t>(ptr), count, x), row, col, p.status);
+#else
+    (void)p; (void)ptr; (void)count; (void)row; (void)col;
+    return true;
+#endif
+}
 
 // Start of FP32 output row `row` (< m): C, or its scatter destination.
 __device__ __forceinline__ float* f32_row(const GemmParams& p, int row) {
@@ -216,12 +232,13 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
                                  __float_as_uint(silu_mul(__uint_as_float(v[i + 10]), __uint_as_float(v[i + 11]))));
                 q.w = pack_half2(__float_as_uint(silu_mul(__uint_as_float(v[i + 12]), __uint_as_float(v[i + 13]))),
                                  __float_as_uint(silu_mul(__uint_as_float(v[i + 14]), __uint_as_float(v[i + 15]))));
-                *reinterpret_cast<uint4*>(crow + (i >> 1)) = q;
+                if (c_span_ok(p, crow + (i >> 1), 8, row, (col0 + i) >> 1))
+                    *reinterpret_cast<uint4*>(crow + (i >> 1)) = q;
             }
         } else {
 #pragma unroll
             for (int i = 0; i < kCnt; i += 2)
-                if (col0 + i < p.n)
+                if (col0 + i < p.n && c_span_ok(p, crow + (i >> 1), 1, row, (col0 + i) >> 1))
                     crow[i >> 1] = __float2half_rn(silu_mul(__uint_as_float(v[i]), __uint_as_float(v[i + 1])));
         }
         return;
@@ -231,11 +248,12 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
         if (p.vec_ok && col0 + kCnt <= p.n) {
 #pragma unroll
             for (int i = 0; i < kCnt; i += 4)
-                *reinterpret_cast<uint4*>(crow + col0 + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                if (c_span_ok(p, crow + col0 + i, 4, row, col0 + i))
+                    *reinterpret_cast<uint4*>(crow + col0 + i) = make_uint4(v[i], v[i + 1], v[i + 2], v[i + 3]);
         } else {
 #pragma unroll
             for (int i = 0; i < kCnt; ++i)
-                if (col0 + i < p.n) crow[col0 + i] = __uint_as_float(v[i]);
+                if (col0 + i < p.n && c_span_ok(p, crow + col0 + i, 1, row, col0 + i)) crow[col0 + i] = __uint_as_float(v[i]);
         }
         return;
     }
@@ -248,12 +266,13 @@ __device__ __forceinline__ void store_row_segment(const GemmParams& p, int row, 
             q.y = pack_half2(v[i + 2], v[i + 3]);
             q.z = pack_half2(v[i + 4], v[i + 5]);
             q.w = pack_half2(v[i + 6], v[i + 7]);
-            *reinterpret_cast<uint4*>(crow + col0 + i) = q;
+            if (c_span_ok(p, crow + col0 + i, 8, row, col0 + i)) *reinterpret_cast<uint4*>(crow + col0 + i) = q;
         }
     } else {
 #pragma unroll
         for (int i = 0; i < kCnt; ++i)
-            if (col0 + i < p.n) crow[col0 + i] = __float2half_rn(__uint_as_float(v[i]));
+            if (col0 + i < p.n && c_span_ok(p, crow + col0 + i, 1, row, col0 + i))
+                crow[col0 + i] = __float2half_rn(__uint_as_float(v[i]));
     }
 }
 
@@ -320,9 +339,8 @@ __device__ __forceinline__ void store_col_segment(const GemmParams& p, int col, 
             float g, u;
             silu_pair(v[j], v[j + 1], odd, g, u);
             const int row = row0 + j + odd;
-            if (col < p.n && row < p.m)
-                static_cast<__half*>(p.c)[static_cast<long long>(row) * p.ldc + (col >> 1)] =
-                    __float2half_rn(silu_mul(g, u));
+            __half* dst = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc + (col >> 1);
+            if (col < p.n && row < p.m && c_span_ok(p, dst, 1, row, col >> 1)) *dst = __float2half_rn(silu_mul(g, u));
         }
         return;
     }
@@ -331,8 +349,13 @@ __device__ __forceinline__ void store_col_segment(const GemmParams& p, int col, 
     for (int j = 0; j < kCnt; ++j) {
         const int row = row0 + j;
         if (row < p.m) {
-            if (p.out_f32) f32_row(p, row)[col] = __uint_as_float(v[j]);
-            else static_cast<__half*>(p.c)[static_cast<long long>(row) * p.ldc + col] = __float2half_rn(__uint_as_float(v[j]));
+            if (p.out_f32) {
+                float* dst = f32_row(p, row) + col;
+                if (c_span_ok(p, dst, 1, row, col)) *dst = __uint_as_float(v[j]);
+            } else {
+                __half* dst = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc + col;
+                if (c_span_ok(p, dst, 1, row, col)) *dst = __float2half_rn(__uint_as_float(v[j]));
+            }
         }
     }
 }
@@ -360,10 +383,10 @@ __device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col
             __half* c = static_cast<__half*>(p.c) + static_cast<long long>(row) * p.ldc + (col >> 1);
             const float h0 = silu_mul(v.x, v.y), h1 = silu_mul(v.z, v.w);
             if (p.vec_ok && col + 4 <= p.n) {
-                *reinterpret_cast<__half2*>(c) = __floats2half2_rn(h0, h1);
+                if (c_span_ok(p, c, 2, row, col >> 1)) *reinterpret_cast<__half2*>(c) = __floats2half2_rn(h0, h1);
             } else {
-                c[0] = __float2half_rn(h0);
-                if (col + 2 < p.n) c[1] = __float2half_rn(h1);
+                if (c_span_ok(p, c, 1, row, col >> 1)) c[0] = __float2half_rn(h0);
+                if (col + 2 < p.n && c_span_ok(p, c + 1, 1, row, (col >> 1) + 1)) c[1] = __float2half_rn(h1);
             }
             return;
         }
@@ -372,12 +395,15 @@ __device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col
     if (p.out_f32) {
         float* c = f32_row(p, row) + col;
         if (p.vec_ok && col + 4 <= p.n) {
-            *reinterpret_cast<float4*>(c) = v;
+            if (c_span_ok(p, c, 4, row, col)) *reinterpret_cast<float4*>(c) = v;
         } else {
-            c[0] = v.x;
-            if (col + 1 < p.n) c[1] = v.y;
-            if (col + 2 < p.n) c[2] = v.z;
-            if (col + 3 < p.n) c[3] = v.w;
+            const int cnt = min(4, p.n - col);
+            if (c_span_ok(p, c, cnt, row, col)) {
+                c[0] = v.x;
+                if (col + 1 < p.n) c[1] = v.y;
+                if (col + 2 < p.n) c[2] = v.z;
+                if (col + 3 < p.n) c[3] = v.w;
+            }
         }
         return;
     }
@@ -386,8 +412,8 @@ __device__ __forceinline__ void store_quad(const GemmParams& p, int row, int col
         uint2 q;
         q.x = pack_half2(__float_as_uint(v.x), __float_as_uint(v.y));
         q.y = pack_half2(__float_as_uint(v.z), __float_as_uint(v.w));
-        *reinterpret_cast<uint2*>(c) = q;
-    } else {
+        if (c_span_ok(p, c, 4, row, col)) *reinterpret_cast<uint2*>(c) = q;
+    } else if (c_span_ok(p, c, min(4, p.n - col), row, col)) {
         c[0] = __float2half_rn(v.x);
         if (col + 1 < p.n) c[1] = __float2half_rn(v.y);
         if (col + 2 < p.n) c[2] = __float2half_rn(v.z);
@@ -472,7 +498,10 @@ struct Piece8 {
     int nv;         // elements of the piece inside the matrix (<= 0: none)
 };
 
-__device__ __forceinline__ Piece8 fetch_piece8(const __half* x, int nv) {
+// `ext` is the operand (debug builds check that each loaded vector holds one
+// of its elements; `i0`, `i1` are the piece's row and column for the record).
+__device__ __forceinline__ Piece8 fetch_piece8(const __half* x, int nv, const Extent& ext, int i0, int i1,
+                                               int* status) {
     Piece8 r;
     r.v0 = make_uint4(0u, 0u, 0u, 0u);
     r.v1 = r.v0;
@@ -480,9 +509,13 @@ __device__ __forceinline__ Piece8 fetch_piece8(const __half* x, int nv) {
     r.off = static_cast<uint32_t>(a & 15u);
     r.nv = nv;
     const uint4* v = reinterpret_cast<const uint4*>(a - r.off);
-    if (nv > 0) r.v0 = __ldg(v);
+    (void)ext; (void)i0; (void)i1; (void)status;
+    if (nv > 0 && HG_DEBUG_OK(vec_touches_matrix(reinterpret_cast<uintptr_t>(v), ext), i0, i1, status))
+        r.v0 = __ldg(v);
     // v1 starts at element (16 - off) / 2 of the piece.
-    if (r.off != 0u && nv > static_cast<int>((16u - r.off) >> 1)) r.v1 = __ldg(v + 1);
+    if (r.off != 0u && nv > static_cast<int>((16u - r.off) >> 1) &&
+        HG_DEBUG_OK(vec_touches_matrix(reinterpret_cast<uintptr_t>(v + 1), ext), i0, i1, status))
+        r.v1 = __ldg(v + 1);
     return r;
 }
 
@@ -518,19 +551,21 @@ __device__ __forceinline__ void load_stage_generic(uint8_t* s_k, uint8_t* s_mn, 
     constexpr int kMNPieces = 64 * kPerRow / 128;
     static_assert(kKRows * 8 % 128 == 0 && 64 * kPerRow % 128 == 0, "whole pieces per thread");
     Piece8 pk[kKPieces], pm[kMNPieces];
+    const Extent ext_a{reinterpret_cast<uintptr_t>(p.a), p.m, p.k, p.lda, 2};
+    const Extent ext_b{reinterpret_cast<uintptr_t>(p.b), p.k, p.n, p.ldb, 2};
 #pragma unroll
     for (int j = 0; j < kKPieces; ++j) {
         const int idx = tid + 128 * j;
         const int gr = r0 + (idx >> 3), gk = k0 + 8 * (idx & 7);
         const int nv = gr < p.m ? min(p.k - gk, 8) : 0;
-        pk[j] = fetch_piece8(p.a + static_cast<long long>(gr) * p.lda + gk, nv);
+        pk[j] = fetch_piece8(p.a + static_cast<long long>(gr) * p.lda + gk, nv, ext_a, gr, gk, p.status);
     }
 #pragma unroll
     for (int j = 0; j < kMNPieces; ++j) {
         const int idx = tid + 128 * j;
         const int gk = k0 + idx / kPerRow, gc = c0 + 8 * (idx % kPerRow);
         const int nv = gk < p.k ? min(p.n - gc, 8) : 0;
-        pm[j] = fetch_piece8(p.b + static_cast<long long>(gk) * p.ldb + gc, nv);
+        pm[j] = fetch_piece8(p.b + static_cast<long long>(gk) * p.ldb + gc, nv, ext_b, gk, gc, p.status);
     }
 #pragma unroll
     for (int j = 0; j < kKPieces; ++j) {
@@ -559,6 +594,12 @@ __global__ void __launch_bounds__(256)
 copy_rows_kernel(const __half* __restrict__ src, long long ld_src, __half* __restrict__ dst,
                  long long ld_dst, long long rows, long long cols) {
     const long long col_step = static_cast<long long>(gridDim.x) * blockDim.x * 8;
+    // Debug builds: reads stay inside the source rows (the aligned source of
+    // a copy-back is the padded staging buffer, its whole pitch owned), writes
+    // inside the destination rows (likewise).
+    const Extent xs{reinterpret_cast<uintptr_t>(src), rows, kDstAligned ? cols : ld_src, ld_src, 2};
+    const Extent xd{reinterpret_cast<uintptr_t>(dst), rows, kDstAligned ? ld_dst : cols, ld_dst, 2};
+    (void)xs; (void)xd;
     for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
         const __half* srow = src + r * ld_src;
         __half* drow = dst + r * ld_dst;
@@ -566,6 +607,10 @@ copy_rows_kernel(const __half* __restrict__ src, long long ld_src, __half* __res
              c += col_step) {
             __align__(16) __half v[8];
             if constexpr (kDstAligned) {
+                if (!HG_DEBUG_OK(span_in_matrix(reinterpret_cast<uintptr_t>(srow + c), min(8LL, cols - c), xs) &&
+                                     span_in_matrix(reinterpret_cast<uintptr_t>(drow + c), 8, xd),
+                                 r, c, nullptr))
+                    continue;
                 if (c + 8 <= cols) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) v[j] = __ldg(srow + c + j);
@@ -575,6 +620,10 @@ copy_rows_kernel(const __half* __restrict__ src, long long ld_src, __half* __res
                 }
                 *reinterpret_cast<uint4*>(drow + c) = *reinterpret_cast<const uint4*>(v);
             } else {
+                if (!HG_DEBUG_OK(span_in_matrix(reinterpret_cast<uintptr_t>(srow + c), 8, xs) &&
+                                     span_in_matrix(reinterpret_cast<uintptr_t>(drow + c), min(8LL, cols - c), xd),
+                                 r, c, nullptr))
+                    continue;
                 *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(srow + c));
 #pragma unroll
                 for (int j = 0; j < 8; ++j)

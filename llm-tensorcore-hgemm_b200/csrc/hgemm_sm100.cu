@@ -1164,6 +1164,7 @@ extern "C" const char* hgemm_sm100_status_string(int status) {
         case HGEMM_SM100_ERR_CUDA: return "CUDA runtime error";
         case HGEMM_SM100_ERR_SCRATCH_LIMIT:
             return "problem needs more scratch than the static buffer (HGEMM_SM100_STATIC_SCRATCH_BYTES)";
+        case HGEMM_SM100_ERR_DEBUG_BOUNDS: return "hgemm: debug bounds check failed";
         default: return "unknown status";
     }
 }
@@ -1180,6 +1181,54 @@ extern "C" int hgemm_sm100_read_status(int32_t* value, int clear) {
     *value = v;
     if (clear && cudaMemset(dev->status_word, 0, sizeof(int)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
     return HGEMM_SM100_OK;
+}
+
+// ============================================================ debug build ==
+
+extern "C" int hgemm_sm100_debug_build(void) {
+#ifdef HGEMM_DEBUG
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+extern "C" int hgemm_sm100_debug_read(int32_t* line, int64_t* index0, int64_t* index1, int clear) {
+    if (line == nullptr || index0 == nullptr || index1 == nullptr) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+    *line = 0;
+    *index0 = *index1 = 0;
+#ifdef HGEMM_DEBUG
+    const DeviceInfo* dev = nullptr;
+    const int rc = device_info(&dev);
+    if (rc != HGEMM_SM100_OK) return rc;
+    if (cudaDeviceSynchronize() != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    DebugRecord rec{};
+    if (cudaMemcpyFromSymbol(&rec, g_debug_record, sizeof(rec)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    *line = rec.line;
+    *index0 = rec.index0;
+    *index1 = rec.index1;
+    if (clear) {
+        const DebugRecord zero{};
+        if (cudaMemcpyToSymbol(g_debug_record, &zero, sizeof(zero)) != cudaSuccess) return HGEMM_SM100_ERR_CUDA;
+    }
+#else
+    (void)clear;
+#endif
+    return HGEMM_SM100_OK;
+}
+
+extern "C" int hgemm_sm100_debug_vec_touches(uint64_t vec, uint64_t base, int64_t rows, int64_t cols, int64_t ld,
+                                             int32_t esize) {
+    if (ld < cols || ld <= 0) return 0;
+    return vec_touches_matrix(static_cast<uintptr_t>(vec), Extent{static_cast<uintptr_t>(base), rows, cols, ld, esize})
+               ? 1 : 0;
+}
+
+extern "C" int hgemm_sm100_debug_span_in(uint64_t ptr, int64_t count, uint64_t base, int64_t rows, int64_t cols,
+                                         int64_t ld, int32_t esize) {
+    if (ld < cols || ld <= 0) return 0;
+    return span_in_matrix(static_cast<uintptr_t>(ptr), count,
+                          Extent{static_cast<uintptr_t>(base), rows, cols, ld, esize}) ? 1 : 0;
 }
 
 // ================================================ static-scratch entry point ==

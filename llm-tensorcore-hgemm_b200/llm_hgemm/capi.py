@@ -11,6 +11,8 @@ import ctypes
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libhgemm_sm100.so"
+# The same library built with -DHGEMM_DEBUG (device-side bounds checks).
+DEBUG_LIB_PATH = Path(__file__).resolve().parent / "libhgemm_sm100_debug.so"
 
 OK = 0
 ERR_INVALID_ARGUMENT = 1
@@ -21,6 +23,7 @@ ERR_PIPELINE_TIMEOUT = 5
 ERR_TENSOR_MAP = 6
 ERR_CUDA = 7
 ERR_SCRATCH_LIMIT = 8
+ERR_DEBUG_BOUNDS = 9
 STATIC_SCRATCH_BYTES = 16 * 1024 * 1024
 
 CFG_AUTO = 0
@@ -86,13 +89,13 @@ class HgemmSm100Scatter(ctypes.Structure):
     ]
 
 
-_lib = None
+_libs: dict[bool, ctypes.CDLL] = {}
 
 
-def load() -> ctypes.CDLL:
-    global _lib
-    if _lib is None:
-        lib = ctypes.CDLL(str(LIB_PATH))
+def load(debug: bool = False) -> ctypes.CDLL:
+    """The kernel library (``debug``: its -DHGEMM_DEBUG build)."""
+    if debug not in _libs:
+        lib = ctypes.CDLL(str(DEBUG_LIB_PATH if debug else LIB_PATH))
         lib.hgemm_sm100_run.argtypes = [ctypes.POINTER(HgemmSm100Args), ctypes.c_void_p]
         lib.hgemm_sm100_run.restype = ctypes.c_int
         lib.hgemm_sm100_resolve.argtypes = [ctypes.POINTER(HgemmSm100Args),
@@ -138,8 +141,19 @@ def load() -> ctypes.CDLL:
         lib.hgemm_sm100_ipc_open.restype = ctypes.c_int
         lib.hgemm_sm100_ipc_close.argtypes = [ctypes.c_void_p]
         lib.hgemm_sm100_ipc_close.restype = ctypes.c_int
-        _lib = lib
-    return _lib
+        lib.hgemm_sm100_debug_build.argtypes = []
+        lib.hgemm_sm100_debug_build.restype = ctypes.c_int
+        lib.hgemm_sm100_debug_read.argtypes = [ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int64),
+                                               ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
+        lib.hgemm_sm100_debug_read.restype = ctypes.c_int
+        lib.hgemm_sm100_debug_vec_touches.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64,
+                                                      ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
+        lib.hgemm_sm100_debug_vec_touches.restype = ctypes.c_int
+        lib.hgemm_sm100_debug_span_in.argtypes = [ctypes.c_uint64, ctypes.c_int64, ctypes.c_uint64, ctypes.c_int64,
+                                                  ctypes.c_int64, ctypes.c_int64, ctypes.c_int32]
+        lib.hgemm_sm100_debug_span_in.restype = ctypes.c_int
+        _libs[debug] = lib
+    return _libs[debug]
 
 
 def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
@@ -158,8 +172,8 @@ def make_args(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, *,
                           epilogue, 0, bias_ptr, residual_ptr, n if ldr is None else ldr)
 
 
-def run(args: HgemmSm100Args, stream: int = 0) -> int:
-    return load().hgemm_sm100_run(ctypes.byref(args), ctypes.c_void_p(stream))
+def run(args: HgemmSm100Args, stream: int = 0, debug: bool = False) -> int:
+    return load(debug).hgemm_sm100_run(ctypes.byref(args), ctypes.c_void_p(stream))
 
 
 def run_static_scratch(args: HgemmSm100Args, stream: int = 0) -> int:
@@ -167,24 +181,41 @@ def run_static_scratch(args: HgemmSm100Args, stream: int = 0) -> int:
     return load().hgemm_sm100_run_static_scratch(ctypes.byref(args), ctypes.c_void_p(stream))
 
 
-def resolve(args: HgemmSm100Args) -> tuple[int, int, int]:
+def resolve(args: HgemmSm100Args, debug: bool = False) -> tuple[int, int, int]:
     cfg, split = ctypes.c_int32(0), ctypes.c_int32(0)
-    rc = load().hgemm_sm100_resolve(ctypes.byref(args), ctypes.byref(cfg), ctypes.byref(split))
+    rc = load(debug).hgemm_sm100_resolve(ctypes.byref(args), ctypes.byref(cfg), ctypes.byref(split))
     return rc, cfg.value, split.value
 
 
-def workspace_size(args: HgemmSm100Args) -> int:
-    return load().hgemm_sm100_workspace_size(ctypes.byref(args))
+def workspace_size(args: HgemmSm100Args, debug: bool = False) -> int:
+    return load(debug).hgemm_sm100_workspace_size(ctypes.byref(args))
 
 
 def status_string(code: int) -> str:
     return load().hgemm_sm100_status_string(code).decode()
 
 
-def read_status(clear: bool = True) -> tuple[int, int]:
+def read_status(clear: bool = True, debug: bool = False) -> tuple[int, int]:
     v = ctypes.c_int32(0)
-    rc = load().hgemm_sm100_read_status(ctypes.byref(v), 1 if clear else 0)
+    rc = load(debug).hgemm_sm100_read_status(ctypes.byref(v), 1 if clear else 0)
     return rc, v.value
+
+
+def debug_read(clear: bool = True, debug: bool = True) -> tuple[int, int, int, int]:
+    """(rc, line, index0, index1) of the first failed bounds check recorded by
+    the debug build (line 0: none)."""
+    line, i0, i1 = ctypes.c_int32(0), ctypes.c_int64(0), ctypes.c_int64(0)
+    rc = load(debug).hgemm_sm100_debug_read(ctypes.byref(line), ctypes.byref(i0), ctypes.byref(i1),
+                                            1 if clear else 0)
+    return rc, line.value, i0.value, i1.value
+
+
+def debug_vec_touches(vec: int, base: int, rows: int, cols: int, ld: int, esize: int = 2) -> bool:
+    return bool(load().hgemm_sm100_debug_vec_touches(vec, base, rows, cols, ld, esize))
+
+
+def debug_span_in(ptr: int, count: int, base: int, rows: int, cols: int, ld: int, esize: int = 2) -> bool:
+    return bool(load().hgemm_sm100_debug_span_in(ptr, count, base, rows, cols, ld, esize))
 
 
 # ------------------------------------------- tensor-parallel row scatter --

@@ -76,3 +76,50 @@ def test_run_rejects_bad_arguments(kwargs, expected):
     assert capi.run(args) == expected
     rc, _, _ = capi.resolve(args)
     assert rc == expected
+
+
+# --------------------------------------------------------- debug build --
+
+@pytest.mark.parametrize("name", declared_functions())
+def test_debug_library_exports(name):
+    assert hasattr(capi.load(debug=True), name), name
+
+
+def test_debug_build_flag_and_empty_record():
+    assert capi.load().hgemm_sm100_debug_build() == 0
+    assert capi.load(debug=True).hgemm_sm100_debug_build() == 1
+    # A release build records nothing and touches no GPU.
+    assert capi.debug_read(debug=False) == (capi.OK, 0, 0, 0)
+    assert re.search(r"\bHGEMM_SM100_ERR_DEBUG_BOUNDS\s*=\s*9\b", HEADER.read_text())
+    assert "debug bounds" in capi.status_string(capi.ERR_DEBUG_BOUNDS)
+
+
+def _elements(base, rows, cols, ld, esize):
+    """Byte addresses of every element of the matrix (a plain restatement)."""
+    return {base + esize * (r * ld + c) for r in range(rows) for c in range(cols)}
+
+
+@pytest.mark.parametrize("base,rows,cols,ld", [(4096, 3, 5, 7), (4098, 4, 9, 9), (4110, 2, 16, 21),
+                                               (4096, 1, 1, 1), (4102, 5, 3, 8)])
+def test_debug_vector_rule_matches_a_brute_force_restatement(base, rows, cols, ld):
+    # The generic loader may load a 16-byte-aligned vector only when it holds
+    # at least one element of its operand.
+    elems = _elements(base, rows, cols, ld, 2)
+    lo, hi = (min(elems) // 16 - 2) * 16, (max(elems) // 16 + 3) * 16
+    for vec in range(lo, hi, 16):
+        expect = any(vec <= e < vec + 16 for e in elems)
+        assert capi.debug_vec_touches(vec, base, rows, cols, ld) == expect, vec
+    assert not capi.debug_vec_touches(lo + 2, base, rows, cols, ld)      # unaligned vectors never pass
+
+
+@pytest.mark.parametrize("esize", [2, 4])
+def test_debug_span_rule_matches_a_brute_force_restatement(esize):
+    base, rows, cols, ld = 8192, 3, 6, 10
+    elems = _elements(base, rows, cols, ld, esize)
+    for ptr in range(base - 4 * esize, base + esize * (rows * ld + 4)):
+        for count in (1, 2, 4, 8):
+            span = {ptr + esize * i for i in range(count)}
+            same_row = (ptr - base) % esize == 0 and ptr >= base and \
+                ((ptr - base) // esize) % ld + count <= ld
+            expect = span <= elems and same_row
+            assert capi.debug_span_in(ptr, count, base, rows, cols, ld, esize) == expect, (ptr, count)
