@@ -185,7 +185,7 @@ def device_time_ms(fn, steps: int, warmup: int, stream, barrier=None) -> float:
 # One sampling rule for the CPU figures (`cpu_baseline` of this arm and every
 # step of `--impl reference`): the reference's CPU path (its oracle: FP32
 # matmul of the FP16 operands, one FP16 rounding) on rows 0..R-1 of A of every
-# GEMM of the workload's step, full N and K, with all of torch's host threads.
+# GEMM of the workload's step, full N and K, with a thread per host core.
 # R is sized from a 64-row probe so that one sampled step takes about
 # CPU_STEP_S seconds; the figure is the sampled FLOPs over the time.
 
@@ -206,7 +206,10 @@ class CpuSample:
         from oracle import reference as oracle
 
         self.oracle = oracle
-        self.threads = torch.get_num_threads()
+        # All of the host's cores (torchrun sets OMP_NUM_THREADS=1 for its
+        # workers; the CPU figures run on rank 0 alone).
+        self.threads = os.cpu_count() or torch.get_num_threads()
+        torch.set_num_threads(self.threads)
         g = torch.Generator().manual_seed(SEED)
         self.bs = [(torch.randn((k, n), generator=g) * 0.1).half() for (_, n, k) in gemms]
         self.gemms = gemms
