@@ -771,6 +771,10 @@ def run_tp_mlp(args, rank: int, world: int, peaks: dict, peak_kind: str) -> dict
     # Fused GEMM + reduce-scatter: the GEMM epilogue stores rows into their
     # owners' buffers over NVLink, one barrier, owners sum their slots.
     variants["p2p_fused_reduce_scatter_ms"] = timed_max(mlp.down_p2p, vsteps)
+    # The step without overlapping the slot reduction with the up-projection.
+    mlp.overlap = False
+    variants["step_without_overlap_ms"] = timed_max(mlp.step, vsteps)
+    mlp.overlap = True
     ref_out = mlp.down_all_reduce().clone()
 
     def shard_ok(shard, rows):

@@ -263,7 +263,7 @@ class TensorParallelMLP:
         self.shard.copy_(self.shard_f32)      # the single FP16 rounding of the owned rows
         return self.shard
 
-    def down_p2p(self, gather: bool = False) -> torch.Tensor:
+    def down_p2p(self, gather: bool = False, during_reduction: Callable | None = None) -> torch.Tensor:
         """Fused GEMM + reduce-scatter over peer memory: returns this rank's
         FP16 [M / G, hidden] shard (rows [r * M / G, (r + 1) * M / G)).
 
@@ -272,7 +272,11 @@ class TensorParallelMLP:
         completes them: the result is the full FP16 [M, hidden] output on
         every rank, the same value an FP32 all-reduce followed by one rounding
         gives (the slots are added in rank order). Its consumers run on this
-        stream; the next call rewrites it."""
+        stream; the next call rewrites it.
+
+        ``during_reduction``: work for the current stream (kernels with no
+        data dependence on this projection) that runs while the slot
+        reduction runs on a side stream."""
         from . import capi
 
         m, hidden = self.partial.shape
@@ -300,6 +304,12 @@ class TensorParallelMLP:
         if self.world > 1:
             # Orders every rank's GEMM (its peer stores) before any owner reads.
             dist.all_reduce(self._barrier_flag, op=dist.ReduceOp.MAX, group=self.group)
+        main = torch.cuda.current_stream(self.x.device)
+        if during_reduction is not None:
+            if getattr(self, "reduce_stream", None) is None:
+                self.reduce_stream = torch.cuda.Stream(device=self.x.device)
+            self.reduce_stream.wait_stream(main)
+            stream = self.reduce_stream.cuda_stream
         if gather:
             offset = self.rank * rows * hidden * 2          # this rank's rows in every output
             outs = [sc.dest[2][q] + offset for q in range(self.world)]
@@ -309,6 +319,9 @@ class TensorParallelMLP:
                                    hidden, stream)
         if rc != capi.OK:
             raise RuntimeError(f"hgemm_sm100_reduce_slots failed: {capi.status_string(rc)}")
+        if during_reduction is not None:
+            during_reduction()
+            main.wait_stream(self.reduce_stream)
         sc.steps += 1
         if not gather:
             return self.shard_p2p
@@ -326,6 +339,18 @@ class TensorParallelMLP:
             self.scatter = None
 
     def step(self) -> None:
+        """One MLP step: the up-projection and the row-parallel
+        down-projection. With several ranks on the fused peer-memory path
+        (``down_mode`` "p2p", ``overlap`` on) the down-projection's exchange is
+        overlapped with the up-projection, which needs no communication: the
+        scatter GEMM runs first, then, after the barrier that orders every
+        rank's stores, the owners' slot reduction and all-gather run on a side
+        stream while the up-projection GEMM runs on the current stream; a
+        second barrier completes the gathered output. The values are the same
+        as ``up()`` then ``down()``."""
+        if self.world > 1 and self.down_mode == "p2p" and getattr(self, "overlap", True) and self.x.is_cuda:
+            self.out = self.down_p2p(gather=True, during_reduction=self.up)
+            return
         self.up()
         self.down()
 
