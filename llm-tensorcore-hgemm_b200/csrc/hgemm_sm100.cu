@@ -639,15 +639,19 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             // shape measured; they win unless their coarser tiles leave a
             // worse last wave. Times below in 128 x 256 K blocks of one SM;
             // the stream-K split tail is charged what it cost when timed
-            // against whole-tile waves (about 40 K blocks).
+            // against whole-tile waves (25 K blocks + 0.4 per K block of a
+            // tile), and the pairs replace it only when 3 % ahead.
             if (tiles >= sms && !(a.flags & HGEMM_SM100_FLAG_OUT_F32)) {
                 const int64_t pairs = sms / 2;
                 const int64_t tiles2 = cdiv(a.m, 256) * cdiv(a.n, 256);
                 const double kb = static_cast<double>(nkb);
-                const double t_pair = static_cast<double>(cdiv(tiles2, pairs)) * kb * 0.94;
-                const double t_one = spread_tail ? static_cast<double>(tiles) / sms * kb + 40.0
-                                                 : static_cast<double>(cdiv(tiles, sms)) * kb;
-                if (t_pair <= t_one) cfg = HGEMM_SM100_CFG_PAIR_256x256;
+                const double t_pair = static_cast<double>(cdiv(tiles2, pairs)) * kb * 0.93;
+                if (spread_tail) {
+                    const double t_sk = static_cast<double>(tiles) / sms * kb + 25.0 + 0.4 * kb;
+                    if (t_pair < 0.97 * t_sk) cfg = HGEMM_SM100_CFG_PAIR_256x256;
+                } else if (t_pair <= static_cast<double>(cdiv(tiles, sms)) * kb) {
+                    cfg = HGEMM_SM100_CFG_PAIR_256x256;
+                }
             }
             // Narrow tiles when they (with their K split) fill the SMs in one
             // wave: the same MMA time per K block, half the partial tile to
