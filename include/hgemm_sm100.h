@@ -72,7 +72,11 @@ enum {
                                               tiles, 64 rows per CTA            */
     HGEMM_SM100_CFG_PAIR_128x128 = 12,     /* "tc_pair_128x128": CTA pair, 128 x 128
                                               tiles, 64 rows per CTA            */
-    HGEMM_SM100_CFG_COUNT = 13
+    HGEMM_SM100_CFG_STREAMK_PAIR_256x256 = 13, /* "tc_streamk_pair_256x256": CTA-pair
+                                              256 x 256 tiles in waves, the last
+                                              partial wave's K blocks spread over
+                                              all pairs (workspace)              */
+    HGEMM_SM100_CFG_COUNT = 14
 };
 
 /* Flags. */

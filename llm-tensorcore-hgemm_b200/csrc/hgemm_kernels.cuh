@@ -2036,4 +2036,317 @@ hgemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_cons
     }
 }
 
+// ======================================== stream-K CTA-pair kernel (256x256) ====
+//
+// The CTA-pair kernel's 256 x 256 tiles with the stream-K work split of
+// hgemm_streamk_kernel: pair g of G processes whole tiles g, g + G, ... in
+// waves, then its equal share of the K blocks of the last (T mod G) + G tiles
+// (each share at least one tile long, so a tile has at most two owners). A
+// share that does not end a tile leaves its FP32 partial in the workspace:
+// each CTA of the pair its own 128 rows, in slot 2 g + rank, published with
+// flag 2 g + rank; the pair owning a tile's last K block adds the partials of
+// the lower-numbered pairs in pair order (deterministic) to its own and
+// stores C. Slots are [quad][row] float4 columns as in hgemm_streamk_kernel,
+// flags hold the launch's epoch while valid and are reset by the finisher.
+// All waits are bounded; the host sizes the grid so that every pair is
+// resident at once.
+
+template <int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+hgemm_pair_streamk_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                          const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+    using Cfg = PairCfg<256, 256, kStages>;
+    constexpr uint32_t kSlotBytes = 128u * 256u * 4u;   // one CTA's FP32 half of a pair tile
+    static_assert(kSlotBytes <= kStages * Cfg::kStageBytes, "a partial slot fits the stage ring");
+    static_assert(2 * kStages + 9 <= 31, "barrier area");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = align_1024(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);   // even CTA
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;      // [2]
+    uint64_t* tempty = tfull + 2;           // [2], even CTA
+    uint64_t* drain = tempty + 2;
+    uint64_t* published = drain + 1;        // 128 epilogue threads wrote this CTA's partial
+    uint64_t* consumed = published + 1;     // 128 epilogue threads read the producers' partials
+    uint64_t* landed = consumed + 1;        // a producer's slot arrived in shared memory
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(landed + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const uint32_t warp = warp_index();
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t rank = cluster_ctarank();   // 0 = MMA CTA, 1 = peer
+    const bool leader = rank == 0;
+
+    if (warp == 4 && lane == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1u);
+            mbar_init(&empty[s], 1u);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1u);
+            mbar_init(&tempty[i], 8u);     // one lane of each epilogue warp, both CTAs
+        }
+        mbar_init(drain, 1u);
+        mbar_init(published, 128u);       // a CTA produces <= 1 partial and finishes <= 1 tile
+        mbar_init(consumed, 128u);
+        mbar_init(landed, 1u);
+        *abort_flag = 0;
+        mbar_init_fence();
+        tma_prefetch_map(&tm_a);
+        tma_prefetch_map(&tm_b);
+    }
+    if (warp == 5) {
+        tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before_sync();
+    cluster_sync();                       // both CTAs' barriers exist before any remote op
+    tc_fence_after_sync();
+    const uint32_t tmem_base = *tmem_slot;
+    grid_dependents_launch();
+    grid_dependency_wait();
+    const WaitCtl wc{abort_flag, p.status, p.timeout_ns};
+
+    const int tiles_m = (p.m + 255) / 256;
+    const int tiles_n = (p.n + 255) / 256;
+    const int T = tiles_m * tiles_n;
+    const int KB = (p.k + kBlockK - 1) / kBlockK;
+    const int G = gridDim.x >> 1;
+    const int g = blockIdx.x >> 1;
+    const int n_sk = p.streamk;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, issued = 0;
+            bool ok = true;
+            SegIter it(g, G, T, KB, n_sk);
+            Seg sg;
+            while (ok && it.next(sg)) {
+                int tm, tn;
+                tile_coords(sg.tile, tiles_m, tiles_n, p.group_m, tm, tn);
+                const int row0 = tm * 256 + static_cast<int>(rank) * Cfg::kRows;
+                const int col0 = tn * 256 + static_cast<int>(rank) * Cfg::kHalfN;
+                for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+                    if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
+                    uint8_t* s_a = smem + stage * Cfg::kStageBytes;
+                    uint8_t* s_b = s_a + Cfg::kABytes;
+                    const uint32_t bar = map_to_rank(smem_addr(&full[stage]), 0);
+                    if (leader) {
+                        const uint32_t extra = (p.inject && issued == 0) ? 16u : 0u;
+                        mbar_arrive_expect_tx(&full[stage], 2u * Cfg::kStageBytes + extra);
+                    }
+                    tma_load_2d_pair(s_a, &tm_a, bar, kb * kBlockK, row0);
+#pragma unroll
+                    for (int j = 0; j < Cfg::kHalfN / 64; ++j)
+                        tma_load_2d_pair(s_b + j * kChunkBytes, &tm_b, bar, col0 + 64 * j, kb * kBlockK);
+                    ++issued;
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            if (leader && (!ok || *abort_flag)) drain_tma<kStages>(full, issued);
+        }
+    } else if (warp == 5) {
+        if (lane == 0 && leader) {
+            uint32_t stage = 0, phase = 0, iter = 0;
+            bool ok = true;
+            SegIter it(g, G, T, KB, n_sk);
+            Seg sg;
+            while (ok && it.next(sg)) {
+                const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+                if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, wc)) { ok = false; break; }
+                tc_fence_after_sync();
+                const uint32_t d = tmem_base + acc * Cfg::kAccCols;
+                for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, wc)) { ok = false; break; }
+                    tc_fence_after_sync();
+                    const uint32_t s_a = smem_addr(smem + stage * Cfg::kStageBytes);
+                    const uint32_t s_b = s_a + Cfg::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBlockK / 16; ++kk)
+                        tc_mma_f16_pair(d, kmaj_desc(s_a, kk), mnmaj_desc(s_b, kk), Cfg::kIdesc,
+                                        (kb > sg.kb0 || kk > 0) ? 1u : 0u);
+                    tc_commit_pair_both(smem_addr(&empty[stage]));
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (ok) tc_commit_pair_both(smem_addr(&tfull[acc]));
+                ++iter;
+            }
+            if (!ok) {
+                tc_commit_pair(smem_addr(drain));
+                mbar_wait_drain(drain, 0, kDrainLimitNs);
+            }
+        }
+    } else if (warp < 4) {
+        const uint32_t t_lane = (warp * 32u) << 16;
+        const int r = warp * 32 + lane;                 // accumulator row of this CTA (TMEM lane)
+        const uint32_t tempty_leader0 = map_to_rank(smem_addr(&tempty[0]), 0);
+        const uint32_t tempty_leader1 = map_to_rank(smem_addr(&tempty[1]), 0);
+        const long long W_sk = static_cast<long long>(n_sk) * KB;
+        const long long base_sk = static_cast<long long>(T - n_sk) * KB;
+        const int slot = 2 * g + static_cast<int>(rank);
+        uint32_t iter = 0, epi_buf = 0;
+        SegIter it(g, G, T, KB, n_sk);
+        Seg sg;
+        while (it.next(sg)) {
+            const uint32_t acc = iter & 1u, acc_phase = (iter >> 1) & 1u;
+            ++iter;
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&tfull[acc], acc_phase, wc))) break;
+            tc_fence_after_sync();
+            int tm, tn;
+            tile_coords(sg.tile, tiles_m, tiles_n, p.group_m, tm, tn);
+            const int row_base = tm * 256 + static_cast<int>(rank) * Cfg::kRows;
+            const uint32_t t_acc = tmem_base + t_lane + acc * Cfg::kAccCols;
+            const bool produce = sg.kb1 < KB;                 // partial owed to a later pair
+            const bool finish = !produce && sg.kb0 > 0;       // adds earlier pairs' partials
+            int p_lo = g;
+            if (finish) {
+                p_lo = sk_owner(static_cast<long long>(sg.tile) * KB - base_sk, G, W_sk);
+                bool ready = true;
+                for (int q = p_lo; q < g && ready; ++q) {
+                    const uint64_t t0 = global_timer_ns();
+                    while (ld_acquire_u64(p.flags + 2 * q + rank) != p.epoch) {
+                        if (*abort_flag || global_timer_ns() - t0 > p.timeout_ns) {
+                            raise_abort(wc, kStatusPipelineTimeout);
+                            ready = false;
+                            break;
+                        }
+                    }
+                }
+                if (!__all_sync(0xffffffffu, ready)) {
+                    tc_fence_before_sync();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+                    break;
+                }
+            }
+            // The finisher segment is this pair's last: the stage ring is idle
+            // (every MMA completed), so a single producer's slot is pulled into
+            // it with bulk copies; with several producers slots are read from
+            // global memory. The sum is (slot p_lo + ... + slot g - 1) + own.
+            const float4* staged = reinterpret_cast<const float4*>(smem);
+            const float4* slots = reinterpret_cast<const float4*>(p.partials);
+            constexpr size_t kSlotQuads = kSlotBytes / 16;
+            float4* my_slot = reinterpret_cast<float4*>(p.partials) + static_cast<size_t>(slot) * kSlotQuads;
+            const bool one_producer = finish && p_lo == g - 1;
+            bool ok_tile = true;
+            if (one_producer) {
+                if (r == 0) {
+                    mbar_arrive_expect_tx(landed, kSlotBytes);
+                    const uint8_t* src = reinterpret_cast<const uint8_t*>(
+                        slots + static_cast<size_t>(2 * p_lo + static_cast<int>(rank)) * kSlotQuads);
+                    for (uint32_t off = 0; off < kSlotBytes; off += 32768u)
+                        bulk_load(smem + off, src + off, 32768u, landed);
+                }
+                ok_tile = __all_sync(0xffffffffu, mbar_wait(landed, 0, wc));
+            }
+            if (ok_tile && p.tma_store && !produce) {
+                uint8_t* boxes = smem + kStages * Cfg::kStageBytes + warp * 8192u;
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 64) {
+                    uint32_t v0[32], v1[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v0);
+                    tmem_ld_32x32b_x32(t_acc + c + 32, v1);
+                    if (finish) {
+                        float4 part[16];
+                        const size_t q0 = static_cast<size_t>(c / 4) * 128u + r;
+                        if (one_producer) {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) part[q] = staged[q0 + static_cast<size_t>(q) * 128u];
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q)
+                                part[q] = __ldcg(slots + static_cast<size_t>(2 * p_lo + static_cast<int>(rank)) * kSlotQuads +
+                                                 q0 + static_cast<size_t>(q) * 128u);
+                            for (int s2 = p_lo + 1; s2 < g; ++s2) {
+#pragma unroll
+                                for (int q = 0; q < 16; ++q) {
+                                    const float4 x = __ldcg(slots + static_cast<size_t>(2 * s2 + static_cast<int>(rank)) *
+                                                                        kSlotQuads + q0 + static_cast<size_t>(q) * 128u);
+                                    part[q].x += x.x; part[q].y += x.y; part[q].z += x.z; part[q].w += x.w;
+                                }
+                            }
+                        }
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            uint32_t* v = q < 8 ? v0 + 4 * q : v1 + 4 * (q - 8);
+                            v[0] = __float_as_uint(part[q].x + __uint_as_float(v[0]));
+                            v[1] = __float_as_uint(part[q].y + __uint_as_float(v[1]));
+                            v[2] = __float_as_uint(part[q].z + __uint_as_float(v[2]));
+                            v[3] = __float_as_uint(part[q].w + __uint_as_float(v[3]));
+                        }
+                    } else {
+                        tmem_wait_ld();
+                    }
+                    epi_add_row<32>(p, row_base + r, tn * 256 + c, v0);
+                    epi_add_row<32>(p, row_base + r, tn * 256 + c + 32, v1);
+                    store_box_tma(&tm_c, boxes + epi_buf * 4096u, lane, v0, v1, tn * 256 + c,
+                                  row_base + static_cast<int>(warp) * 32);
+                    epi_buf ^= 1u;
+                }
+            } else if (ok_tile) {
+#pragma unroll 1
+                for (int c = 0; c < 256; c += 32) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(t_acc + c, v);
+                    tmem_wait_ld();
+                    if (produce) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            my_slot[((c + j) / 4) * 128 + r] = make_float4(
+                                __uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                __uint_as_float(v[j + 3]));
+                        continue;
+                    }
+                    if (finish) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            const size_t qi = static_cast<size_t>((c + j) / 4) * 128u + r;
+                            float4 sum;
+                            if (one_producer) {
+                                sum = staged[qi];
+                            } else {
+                                sum = __ldcg(slots + static_cast<size_t>(2 * p_lo + static_cast<int>(rank)) * kSlotQuads + qi);
+                                for (int q = p_lo + 1; q < g; ++q) {
+                                    const float4 x = __ldcg(slots + static_cast<size_t>(2 * q + static_cast<int>(rank)) *
+                                                                        kSlotQuads + qi);
+                                    sum.x += x.x; sum.y += x.y; sum.z += x.z; sum.w += x.w;
+                                }
+                            }
+                            v[j] = __float_as_uint(sum.x + __uint_as_float(v[j]));
+                            v[j + 1] = __float_as_uint(sum.y + __uint_as_float(v[j + 1]));
+                            v[j + 2] = __float_as_uint(sum.z + __uint_as_float(v[j + 2]));
+                            v[j + 3] = __float_as_uint(sum.w + __uint_as_float(v[j + 3]));
+                        }
+                    }
+                    store_row_segment<32>(p, row_base + r, tn * 256 + c, v);
+                }
+            }
+            tc_fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
+            if (!ok_tile) break;
+            if (produce) {
+                __threadfence();
+                mbar_arrive(published);
+                if (r == 0 && mbar_wait(published, 0, wc)) st_release_u64(p.flags + slot, p.epoch);
+            } else if (finish) {
+                mbar_arrive(consumed);
+                if (r == 0 && mbar_wait(consumed, 0, wc))
+                    for (int q = p_lo; q < g; ++q) p.flags[2 * q + rank] = 0ull;
+            }
+        }
+        if (p.tma_store && lane == 0) bulk_wait_group_all();
+    }
+
+    __syncwarp();
+    if (*abort_flag) settle_ns(2000000ull);
+    tc_fence_before_sync();
+    cluster_sync();                       // no CTA leaves while its pair may still touch it
+    if (warp == 5) {
+        tc_fence_after_sync();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
 }  // namespace hgemm

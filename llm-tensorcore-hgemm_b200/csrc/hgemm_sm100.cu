@@ -53,6 +53,7 @@ const char* const kConfigNames[HGEMM_SM100_CFG_COUNT] = {
     "tc_pair_256x128",
     "tc_pair_128x256",
     "tc_pair_128x128",
+    "tc_streamk_pair_256x256",
 };
 
 // ------------------------------------------------------ device properties --
@@ -217,6 +218,8 @@ KernelEntry g_pair_256 = HG_PAIR(256, 256, 6);
 KernelEntry g_pair_128 = HG_PAIR(256, 128, 8);
 KernelEntry g_pair_m128_256 = HG_PAIR(128, 256, 8);
 KernelEntry g_pair_m128_128 = HG_PAIR(128, 128, 12);
+KernelEntry g_pair_sk_256 = KernelEntry{reinterpret_cast<const void*>(&hgemm_pair_streamk_kernel<6>),
+                                        PairCfg<256, 256, 6>::kSmemBytes};
 KernelEntry g_sk_256 = HG_STREAMK(256, false, 4);
 KernelEntry g_sk_swap_16 = HG_STREAMK(16, true, 10);
 KernelEntry g_sk_swap_32 = HG_STREAMK(32, true, 9);
@@ -464,11 +467,27 @@ struct StreamKPlan {
 };
 
 bool is_streamk(int32_t cfg) {
-    return cfg == HGEMM_SM100_CFG_STREAMK_128x256 || cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB;
+    return cfg == HGEMM_SM100_CFG_STREAMK_128x256 || cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB ||
+           cfg == HGEMM_SM100_CFG_STREAMK_PAIR_256x256;
 }
 
 StreamKPlan plan_streamk(int32_t cfg, int64_t m, int64_t n, int64_t k, int sms) {
     StreamKPlan sp;
+    if (cfg == HGEMM_SM100_CFG_STREAMK_PAIR_256x256) {
+        // Pairs of CTAs (grid = 2 x pairs), one 128-row half of a 256 x 256
+        // partial tile per CTA slot, one flag per CTA.
+        const int pairs = sms / 2;
+        sp.k = &g_pair_sk_256;
+        sp.bnm = 256;
+        sp.tiles = cdiv(m, 256) * cdiv(n, 256);
+        sp.kb = cdiv(k, kBlockK);
+        const int64_t rem = sp.tiles % pairs;
+        sp.streamk = (sp.tiles >= pairs && rem != 0) ? static_cast<int>(rem + pairs) : 0;
+        sp.grid = 2 * static_cast<int>(sp.tiles < pairs ? sp.tiles : pairs);
+        sp.slot_bytes = static_cast<size_t>(128) * 256 * 4;
+        sp.bytes = sp.streamk ? static_cast<size_t>(sp.grid) * (sp.slot_bytes + 8) + 512 : 0;
+        return sp;
+    }
     if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB) {
         sp.swap = true;
         if (m <= 16) { sp.bnm = 16; sp.k = &g_sk_swap_16; }
@@ -646,11 +665,19 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
                 const int64_t tiles2 = cdiv(a.m, 256) * cdiv(a.n, 256);
                 const double kb = static_cast<double>(nkb);
                 const double t_pair = static_cast<double>(cdiv(tiles2, pairs)) * kb * 0.93;
-                if (spread_tail) {
-                    const double t_sk = static_cast<double>(tiles) / sms * kb + 25.0 + 0.4 * kb;
-                    if (t_pair < 0.97 * t_sk) cfg = HGEMM_SM100_CFG_PAIR_256x256;
-                } else if (t_pair <= static_cast<double>(cdiv(tiles, sms)) * kb) {
+                double t_best = spread_tail ? static_cast<double>(tiles) / sms * kb + 25.0 + 0.4 * kb
+                                            : static_cast<double>(cdiv(tiles, sms)) * kb;
+                if (spread_tail ? t_pair < 0.97 * t_best : t_pair <= t_best) {
                     cfg = HGEMM_SM100_CFG_PAIR_256x256;
+                    t_best = t_pair;
+                }
+                // Stream-K over pairs: whole pair-tile waves, then the partial
+                // last wave's K blocks spread over every pair; its fixup cost
+                // measured 10 + 0.47 K blocks. It pays off when the last wave
+                // of 256 x 256 tiles is nearly empty.
+                if (tiles2 >= pairs && tiles2 % pairs != 0) {
+                    const double t_psk = static_cast<double>(tiles2) / pairs * kb * 0.93 + 10.0 + 0.47 * kb;
+                    if (t_psk < 0.97 * t_best) cfg = HGEMM_SM100_CFG_STREAMK_PAIR_256x256;
                 }
             }
             // Narrow tiles when they (with their K split) fill the SMs in one
@@ -669,8 +696,9 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
         const size_t need = align_up(st.total, kStageAlign) + sp.bytes;
         const size_t have = a.workspace != nullptr ? a.workspace_bytes : 0;
         if (sp.bytes > 0 && have < need)
-            cfg = cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB ? HGEMM_SM100_CFG_SWAPAB
-                                                        : HGEMM_SM100_CFG_PERSISTENT_128x256;
+            cfg = cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB        ? HGEMM_SM100_CFG_SWAPAB
+                  : cfg == HGEMM_SM100_CFG_STREAMK_PAIR_256x256 ? HGEMM_SM100_CFG_PAIR_256x256
+                                                                : HGEMM_SM100_CFG_PERSISTENT_128x256;
     }
 
     int32_t split = 1;
@@ -899,6 +927,23 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             const dim3 grid(static_cast<unsigned>(cdiv(a.n, 128)),
                             static_cast<unsigned>(cdiv(a.m, sc.bnm)), static_cast<unsigned>(split));
             return launch(*sc.k, grid, split, map_k, map_mn, map_c, p, stream);
+        }
+        case HGEMM_SM100_CFG_STREAMK_PAIR_256x256: {
+            const StreamKPlan sp = plan_streamk(cfg, a.m, a.n, a.k, dev.sms);
+            if ((rc = tensor_map(&map_k, a.a, K, M, a.lda, 64, 128)) != HGEMM_SM100_OK) return rc;
+            if ((rc = tensor_map(&map_mn, a.b, N, K, a.ldb, 64, 64)) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
+            if ((rc = prepare_kernel(*sp.k, devid)) != HGEMM_SM100_OK) return rc;
+            p.streamk = sp.streamk;
+            p.group_m = 8;
+            if (sp.streamk) {
+                if (region == nullptr || region_bytes < sp.bytes) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
+                p.partials = reinterpret_cast<float*>(region);
+                p.flags = reinterpret_cast<unsigned long long*>(region +
+                                                                static_cast<size_t>(sp.grid) * sp.slot_bytes);
+                p.epoch = next_epoch();
+            }
+            return launch(*sp.k, dim3(static_cast<unsigned>(sp.grid), 1, 1), 1, map_k, map_mn, map_c, p, stream, 2);
         }
         case HGEMM_SM100_CFG_STREAMK_128x256:
         case HGEMM_SM100_CFG_STREAMK_SWAPAB: {
@@ -1257,7 +1302,7 @@ extern "C" int hgemm_sm100_run_static_scratch(const HgemmSm100Args* args, void* 
     const bool automatic = args->config == HGEMM_SM100_CFG_AUTO;
     int32_t cfg = args->config;
     if (automatic) cfg = args->m <= 128 ? HGEMM_SM100_CFG_STREAMK_SWAPAB : HGEMM_SM100_CFG_STREAMK_128x256;
-    if (!is_streamk(cfg)) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
+    if (!is_streamk(cfg) || cfg == HGEMM_SM100_CFG_STREAMK_PAIR_256x256) return HGEMM_SM100_ERR_UNKNOWN_CONFIG;
     if (cfg == HGEMM_SM100_CFG_STREAMK_SWAPAB && args->m > 128) cfg = HGEMM_SM100_CFG_STREAMK_128x256;
 
     const StreamKPlan sp = plan_streamk(cfg, args->m, args->n, args->k, dev->sms);

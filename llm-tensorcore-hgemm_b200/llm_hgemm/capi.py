@@ -39,6 +39,7 @@ CFG_STREAMK_SWAPAB = 9
 CFG_PAIR_256x128 = 10
 CFG_PAIR_128x256 = 11
 CFG_PAIR_128x128 = 12
+CFG_STREAMK_PAIR_256x256 = 13
 
 FLAG_OUT_F32 = 1
 FLAG_TEST_INJECT_TX = 2

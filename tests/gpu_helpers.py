@@ -20,6 +20,7 @@ IMPLEMENTATIONS = [
     "tc_pair_256x128",
     "tc_pair_128x256",
     "tc_pair_128x128",
+    "tc_streamk_pair_256x256",
 ]
 
 

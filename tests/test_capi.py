@@ -31,7 +31,7 @@ def test_library_exports(name):
 def test_config_names_round_trip():
     lib = capi.load()
     n = lib.hgemm_sm100_num_configs()
-    assert n == 13
+    assert n == 14
     for i in range(n):
         name = lib.hgemm_sm100_config_name(i).decode()
         assert lib.hgemm_sm100_config_from_name(name.encode()) == i

@@ -28,6 +28,7 @@ CONFIG_IDS = {
     "tc_pair_256x128": capi.CFG_PAIR_256x128,
     "tc_pair_128x256": capi.CFG_PAIR_128x256,
     "tc_pair_128x128": capi.CFG_PAIR_128x128,
+    "tc_streamk_pair_256x256": capi.CFG_STREAMK_PAIR_256x256,
 }
 
 

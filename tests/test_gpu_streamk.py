@@ -29,7 +29,8 @@ SK_SHAPES = [
     (300, 520, 2056),      # plain: 9 tiles < SMs, whole tiles only
 ]
 CONFIGS = {"tc_streamk_128x256": capi.CFG_STREAMK_128x256,
-           "tc_streamk_swapab": capi.CFG_STREAMK_SWAPAB}
+           "tc_streamk_swapab": capi.CFG_STREAMK_SWAPAB,
+           "tc_streamk_pair_256x256": capi.CFG_STREAMK_PAIR_256x256}
 
 
 @pytest.fixture(autouse=True, scope="module")
@@ -66,7 +67,8 @@ def test_streamk_gate_and_determinism(config, shape):
 @pytest.mark.parametrize("config,mn", [
     ("tc_streamk_swapab", (1, 19200)), ("tc_streamk_swapab", (16, 151936)),
     ("tc_streamk_128x256", (2048, 2560)), ("tc_streamk_128x256", (8192, 5120)),
-    ("tc_streamk_128x256", (4736, 1280))])
+    ("tc_streamk_128x256", (4736, 1280)), ("tc_streamk_pair_256x256", (2048, 2560)),
+    ("tc_streamk_pair_256x256", (8192, 5120)), ("tc_streamk_pair_256x256", (4736, 1280))])
 @pytest.mark.parametrize("kblocks", [1, 2, 45])
 def test_streamk_stage_markers(config, mn, kblocks):
     m, n = mn
@@ -110,7 +112,7 @@ TILE_KERNELS = ("tc_swapab", "tc_splitk_128x256")
 
 @pytest.mark.parametrize("shape,expected", [
     ((1, 151936, 2560), ("tc_streamk_swapab",)), ((16, 4096, 2560), ("tc_swapab",)),
-    ((2048, 2560, 4096), ("tc_streamk_128x256",)), ((512, 2560, 4096), TILE_KERNELS),
+    ((2048, 2560, 4096), ("tc_streamk_pair_256x256",)), ((512, 2560, 4096), TILE_KERNELS),
     ((512, 4096, 2560), TILE_KERNELS), ((512, 1024, 2560), TILE_KERNELS),
     ((200, 2560, 9728), TILE_KERNELS), ((8192, 8192, 1024), ("tc_pair_256x256",))])
 def test_auto_picks_streamk_when_tiles_fill_the_sms(shape, expected):
@@ -118,3 +120,35 @@ def test_auto_picks_streamk_when_tiles_fill_the_sms(shape, expected):
     cfg, _ = resolved_config(a, b, "auto")
     assert cfg in expected, (shape, cfg)
     assert_gate(hgemm(a, b), a, b)
+
+
+@pytest.mark.parametrize("shape", [(2048, 2560, 4096), (4096, 4096, 4096), (8192, 2560, 1000)])
+def test_streamk_pair_graph_replay_and_single_launch(shape):
+    """The CTA-pair stream-K configuration: a split tail is planned (workspace
+    > 0), results pass the gate, match between two eager launches bitwise, and
+    replays of one captured launch see their own flags."""
+    m, n, k = shape
+    a, b = seeded_inputs(m, n, k)
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    need = capi_run(a, b, out, capi.CFG_STREAMK_PAIR_256x256)
+    assert need > 0
+    assert_gate(out, a, b)
+    out2 = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float16)
+    capi_run(a, b, out2, capi.CFG_STREAMK_PAIR_256x256)
+    assert torch.equal(out, out2)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        _hgemm_out(a, b, out, implementation="tc_streamk_pair_256x256")
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _hgemm_out(a, b, out, implementation="tc_streamk_pair_256x256")
+    for seed in (1, 2):
+        torch.manual_seed(seed)
+        a.copy_(torch.randn_like(a) * 0.1)
+        b.copy_(torch.randn_like(b) * 0.1)
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert_gate(out, a, b)

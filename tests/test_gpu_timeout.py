@@ -28,6 +28,7 @@ TMA_CONFIGS = {
     "tc_swapab": (capi.CFG_SWAPAB, (16, 512, 1024)),
     "tc_streamk_128x256": (capi.CFG_STREAMK_128x256, (300, 520, 2056)),
     "tc_streamk_swapab": (capi.CFG_STREAMK_SWAPAB, (8, 1000, 3000)),
+    "tc_streamk_pair_256x256": (capi.CFG_STREAMK_PAIR_256x256, (512, 512, 512)),
 }
 
 
