@@ -41,6 +41,7 @@ CUSTOM_PROVIDERS = (
     "tc_pair_256x128",
     "tc_pair_128x256",
     "tc_pair_128x128",
+    "tc_streamk_pair_256x256",
 )
 MISALIGNED_PROVIDER = "auto"
 DEFAULT_PROVIDER = "auto"
