@@ -1215,6 +1215,14 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
     tn = in / gsz;
 }
 
+// Inverse of tile_coords without rotation: the raster index of tile (tm, tn).
+__device__ __forceinline__ int tile_index(int tm, int tn, int tiles_m, int tiles_n, int group_m) {
+    const int g = tm / group_m;
+    const int first_m = g * group_m;
+    const int gsz = min(tiles_m - first_m, group_m);
+    return g * group_m * tiles_n + tn * gsz + (tm - first_m);
+}
+
 // M-tile rotation of a row scatter: rank r starts on the rows of rank r + 1,
 // so that at any time each owner receives from about one peer instead of
 // all of them writing into the same owner's buffer (NVLink incast).
@@ -1405,6 +1413,14 @@ hgemm_persistent_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_c
 // empty" and "accumulator full" to the barriers of both CTAs with one
 // multicast commit each; one lane per
 // epilogue warp of either CTA arrives on the even CTA's "accumulator empty".
+// Pairs step through the tiles in waves (pair g takes tiles g, g + G, ...);
+// odd waves walk K from the last block down, so that a tile starts on the
+// A rows / B columns the previous wave's tiles in the same raster group
+// read last, while they are still in L2 (at 8192^3: 1.06 -> 0.93 GB read
+// from DRAM per launch). The MMA side only counts K blocks, so the order
+// changes nothing but the FP32 summation order of a tile. The direction is
+// that of the output tile's wave in the unrotated raster, so a row-scatter
+// launch (rows rotated per rank) sums every tile exactly as a plain launch.
 
 template <int kTileMT, int kTileNT, int kStages>
 struct PairCfg {
@@ -1495,7 +1511,10 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                 tile_coords(t, tiles_m, tiles_n, p.group_m, tm, tn, m_rot);
                 const int row0 = tm * Cfg::kTileM + static_cast<int>(rank) * Cfg::kRows;
                 const int col0 = tn * Cfg::kTileN + static_cast<int>(rank) * Cfg::kHalfN;
-                for (int kb = 0; kb < nkb; ++kb) {
+                const int t_out = m_rot != 0 ? tile_index(tm, tn, tiles_m, tiles_n, p.group_m) : t;
+                const bool backwards = ((t_out / npairs) & 1) != 0;
+                for (int kq = 0; kq < nkb; ++kq) {
+                    const int kb = backwards ? nkb - 1 - kq : kq;
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
                     uint8_t* s_a = smem + stage * Cfg::kStageBytes;
                     uint8_t* s_b = s_a + Cfg::kABytes;

@@ -454,6 +454,22 @@ int check_args(const HgemmSm100Args* a) {
     return HGEMM_SM100_OK;
 }
 
+// Raster group height (tile rows) of the CTA-pair kernels. A wave of P pair
+// tiles spans about g rows and P / g columns of 256 x 256 tiles; the next
+// wave of the same group re-reads those A rows, and every group re-reads all
+// of B. Taller groups read B fewer times but push the previous wave's A rows
+// further back in L2: the tallest of 8, 16, 32 whose one-wave footprint,
+// (g + P / g) panels of 256 x K halves, stays within 48 MB (what kept the
+// reuse in L2 when timed; 8 when none does, e.g. K = 8192).
+int pair_group_m(int32_t cfg, int64_t m, int64_t k, int pairs) {
+    int g = 8;
+    if (cfg != HGEMM_SM100_CFG_PAIR_256x256) return g;
+    const double panel = 512.0 * static_cast<double>(k);
+    for (int h : {16, 32})
+        if (h <= cdiv(m, 256) && (h + static_cast<double>(pairs) / h) * panel <= 48e6) g = h;
+    return g;
+}
+
 // Stream-K configurations: tile geometry, grid and workspace of one launch.
 struct StreamKPlan {
     KernelEntry* k = nullptr;
@@ -900,7 +916,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             const int64_t tiles = cdiv(a.m, tm) * cdiv(a.n, tn);
             const int64_t pairs_max = dev.sms / 2;
             const int64_t pairs = tiles < pairs_max ? tiles : pairs_max;
-            p.group_m = 8;
+            p.group_m = pair_group_m(cfg, a.m, a.k, static_cast<int>(pairs_max));
             return launch(k, dim3(static_cast<unsigned>(2 * pairs), 1, 1), 1, map_k, map_mn, map_c, p, stream, 2);
         }
         case HGEMM_SM100_CFG_SPLITK_128x128:
