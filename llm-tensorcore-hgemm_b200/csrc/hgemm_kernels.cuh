@@ -94,7 +94,7 @@ struct GemmParams {
     // rank q = i / sc_rows, sc_dest[q] (a peer GPU's memory for q != sc_rank),
     // at row i - q * sc_rows of that slot.
     int sc_ranks, sc_rank, sc_rows;
-    int sc_bulk;               // rows leave through cp.async.bulk (persistent kernel)
+    int sc_bulk;               // rows leave through cp.async.bulk (persistent and pair kernels)
     long long sc_ld;
     float* sc_dest[8];
 };
@@ -1600,7 +1600,9 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(t_acc + c, v);
                     tmem_wait_ld();
-                    if (p.sc_ranks > 0)
+                    if (p.sc_bulk)
+                        store_block_f32_bulk(p, boxes, buf, lane, v, row0, col0 + c);
+                    else if (p.sc_ranks > 0)
                         store_block_f32(p, reinterpret_cast<float*>(boxes), lane, v, row0, col0 + c);
                     else
                         store_row_segment<32>(p, row0 + static_cast<int>(lane), col0 + c, v);
@@ -1611,6 +1613,7 @@ hgemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constan
             if (lane == 0) mbar_arrive_cluster(acc ? tempty_leader1 : tempty_leader0);
         }
         if (p.tma_store && lane == 0) bulk_wait_group_all();
+        if (p.sc_bulk) bulk_wait_group_all();     // every lane's row copies have landed
     }
 
     __syncwarp();

@@ -668,15 +668,16 @@ int resolve_cfg(const HgemmSm100Args& a, const DeviceInfo& dev, bool assume_work
             cfg = tiles < sms      ? HGEMM_SM100_CFG_SPLITK_128x256
                   : spread_tail    ? HGEMM_SM100_CFG_STREAMK_128x256
                                    : HGEMM_SM100_CFG_PERSISTENT_128x256;
-            // CTA pairs on 256 x 256 tiles (FP16 output): each SM streams 32
-            // instead of 48 KB per K block for the same MMA work, which ran
-            // 5-7 % faster per tile than the 1-CTA kernel on every large
-            // shape measured; they win unless their coarser tiles leave a
-            // worse last wave. Times below in 128 x 256 K blocks of one SM;
+            // CTA pairs on 256 x 256 tiles: each SM streams 32 instead of
+            // 48 KB per K block for the same MMA work, which ran 5-7 % faster
+            // per tile than the 1-CTA kernel on every large FP16-output shape
+            // measured and 7-20 % faster with FP32 output (the tensor-parallel
+            // down-projection partials, 8192 x 2560 x 2432 .. 9728); they win
+            // unless their coarser tiles leave a worse last wave. Times below in 128 x 256 K blocks of one SM;
             // the stream-K split tail is charged what it cost when timed
             // against whole-tile waves (25 K blocks + 0.4 per K block of a
             // tile), and the pairs replace it only when 3 % ahead.
-            if (tiles >= sms && !(a.flags & HGEMM_SM100_FLAG_OUT_F32)) {
+            if (tiles >= sms) {
                 const int64_t pairs = sms / 2;
                 const int64_t tiles2 = cdiv(a.m, 256) * cdiv(a.n, 256);
                 const double kb = static_cast<double>(nkb);
@@ -852,9 +853,11 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
         }
         p.vec_ok = aligned;
         // Bulk row copies: 16-byte-aligned rows (aligned above) of whole 16-byte
-        // pieces; the persistent kernels use them.
+        // pieces; the persistent and CTA-pair kernels use them.
         p.sc_bulk = aligned && a.n % 4 == 0 &&
-                    (cfg == HGEMM_SM100_CFG_PERSISTENT_128x256 || cfg == HGEMM_SM100_CFG_PERSISTENT_128x128);
+                    (cfg == HGEMM_SM100_CFG_PERSISTENT_128x256 || cfg == HGEMM_SM100_CFG_PERSISTENT_128x128 ||
+                     cfg == HGEMM_SM100_CFG_PAIR_256x256 || cfg == HGEMM_SM100_CFG_PAIR_256x128 ||
+                     cfg == HGEMM_SM100_CFG_PAIR_128x256 || cfg == HGEMM_SM100_CFG_PAIR_128x128);
     }
     p.epi_vec = (p.epi & HGEMM_SM100_EPI_BIAS ? reinterpret_cast<uintptr_t>(a.bias) % 16 == 0 : true) &&
                 (p.epi & HGEMM_SM100_EPI_RESIDUAL
@@ -1028,6 +1031,14 @@ int run_impl(const HgemmSm100Args* args, const HgemmSm100Scatter* sc, void* stre
     int32_t cfg = 0, split = 1;
     rc = resolve(*args, *dev, &cfg, &split);
     if (rc != HGEMM_SM100_OK) return rc;
+    // A row scatter's FP32 rows leave through bulk copies in the epilogue; with
+    // short K that epilogue weighs more in the CTA-pair kernel than in the
+    // 1-CTA persistent one (8192 x 2560 partials, K = 1216 / 2432: pairs 10 % /
+    // 3 % slower; K = 4864 and 8192 x 8192 partials, K = 3584 .. 14336: 3-6 %
+    // faster), so `auto` keeps the 1-CTA kernel below K = 3072.
+    if (sc != nullptr && args->config == HGEMM_SM100_CFG_AUTO && args->k < 3072 &&
+        (cfg == HGEMM_SM100_CFG_PAIR_256x256 || cfg == HGEMM_SM100_CFG_STREAMK_PAIR_256x256))
+        cfg = HGEMM_SM100_CFG_PERSISTENT_128x256;
 
     // Workspace layout: [staging buffers][kernel region: stream-K partial
     // slots + flags, or split-K exchange slots].

@@ -117,7 +117,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _p2p_worker(rank, world, port, results):
+def _p2p_worker(rank, world, port, results, shape=(1024, 768, 2048)):
     import torch.distributed as dist
     from datetime import timedelta
 
@@ -128,8 +128,9 @@ def _p2p_worker(rank, world, port, results):
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
-        mlp = TensorParallelMLP.synthetic(rank, world, seed=9, device=torch.device("cuda", rank), m=1024,
-                                          hidden=768, inter=2048)
+        m, hidden, inter = shape
+        mlp = TensorParallelMLP.synthetic(rank, world, seed=9, device=torch.device("cuda", rank), m=m,
+                                          hidden=hidden, inter=inter)
         full = mlp.down_all_reduce().clone()
         ref = full[mlp.owned_rows(1).to(full.device)]
         worst = 0.0
@@ -153,13 +154,16 @@ def _p2p_worker(rank, world, port, results):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_fused_reduce_scatter_matches_all_reduce():
+@pytest.mark.parametrize("shape", [(1024, 768, 2048), (8192, 2560, 9728)], ids=["small", "qwen3_4b_mlp"])
+def test_two_gpu_fused_reduce_scatter_matches_all_reduce(shape):
+    """The small MLP runs the tile kernels; the Qwen3-4B MLP (K = 4864 per rank) the
+    CTA-pair kernel with its bulk-copy row scatter across NVLink."""
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     results = ctx.Manager().dict()
     port = _free_port()
-    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, results)) for r in range(2)]
+    procs = [ctx.Process(target=_p2p_worker, args=(r, 2, port, results, shape)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
