@@ -23,23 +23,38 @@ def single_thread():
     torch.set_num_threads(saved)
 
 
+def _impl(name):
+    """The test-side oracle, or the package's public gate API (llm_hgemm.reference):
+    both restate the reference's llm_hgemm/reference.py and both are pinned to the
+    fixtures it generated."""
+    if name == "oracle":
+        return oracle
+    from llm_hgemm import reference as public
+    return public
+
+
+IMPLS = ["oracle", "llm_hgemm.reference"]
+
+
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_oracle_matches_reference_outputs(golden, shape):
+def test_oracle_matches_reference_outputs(golden, shape, impl):
     tag = "x".join(map(str, shape))
     a = torch.from_numpy(golden[f"a_{tag}"])
     b = torch.from_numpy(golden[f"b_{tag}"])
     expected = golden[f"c_{tag}"]
-    out = oracle.torch_reference(a, b).numpy()
+    out = _impl(impl).torch_reference(a, b).numpy()
     assert out.dtype == np.float16 and out.shape == expected.shape
     # Same FP32 GEMM then one FP16 rounding: bit-identical on the same CPU.
     np.testing.assert_array_equal(out.view(np.uint16), expected.view(np.uint16))
 
 
+@pytest.mark.parametrize("impl", IMPLS)
 @pytest.mark.parametrize("pattern", ["uniform", "sparse"])
-def test_oracle_input_patterns(golden, pattern):
+def test_oracle_input_patterns(golden, pattern, impl):
     a = torch.from_numpy(golden[f"a_{pattern}"])
     b = torch.from_numpy(golden[f"b_{pattern}"])
-    out = oracle.torch_reference(a, b).numpy()
+    out = _impl(impl).torch_reference(a, b).numpy()
     np.testing.assert_array_equal(out.view(np.uint16), golden[f"c_{pattern}"].view(np.uint16))
 
 
@@ -49,19 +64,21 @@ def test_zero_inputs_give_zero():
     assert torch.count_nonzero(oracle.torch_reference(a, b)) == 0
 
 
-def test_error_metrics_match_reference(golden):
+@pytest.mark.parametrize("impl", IMPLS)
+def test_error_metrics_match_reference(golden, impl):
+    gate = _impl(impl)
     spec = json.loads((GOLDEN / "metrics_golden.json").read_text())
     base = torch.from_numpy(golden[spec["base"]])
     outs = perturbations(base)
     for case in spec["cases"]:
-        metrics = oracle.error_metrics(outs[case["name"]], base)
+        metrics = gate.error_metrics(outs[case["name"]], base)
         for key, value in case["metrics"].items():
             got = metrics[key]
             if isinstance(value, float) and math.isnan(value):
                 assert math.isnan(got), (case["name"], key)
             else:
                 assert got == value, (case["name"], key, got, value)
-        assert oracle.correctness_passed(metrics) == case["passed"], case["name"]
+        assert gate.correctness_passed(metrics) == case["passed"], case["name"]
 
 
 def test_stage_marker_known_answer():
