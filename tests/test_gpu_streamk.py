@@ -152,3 +152,22 @@ def test_streamk_pair_graph_replay_and_single_launch(shape):
         graph.replay()
         torch.cuda.synchronize()
         assert_gate(out, a, b)
+
+
+@pytest.mark.parametrize("shape", [(8192, 2560, 4864), (2100, 2600, 1000), (4096, 8192, 3584)],
+                         ids=lambda s: "x".join(map(str, s)))
+def test_auto_fp32_output_takes_cta_pairs(shape):
+    """FP32 output (the tensor-parallel partials) resolves to the CTA-pair kernels
+    from one wave of tiles up, like FP16 output, and matches the FP32 product."""
+    from llm_hgemm.ops import hgemm_f32_out
+
+    m, n, k = shape
+    a, b = seeded_inputs(m, n, k)
+    out = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
+    args = capi.make_args(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, flags=capi.FLAG_OUT_F32)
+    rc, cfg, _ = capi.resolve(args)
+    assert rc == capi.OK and cfg in (capi.CFG_PAIR_256x256, capi.CFG_STREAMK_PAIR_256x256), (shape, cfg)
+    hgemm_f32_out(a, b, out, implementation="auto")
+    assert not torch.backends.cuda.matmul.allow_tf32
+    ref = a.float() @ b.float()
+    torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
