@@ -81,6 +81,21 @@ def test_emulated_scatter_equals_rank_order_sum(config, world, shape):
     assert oracle.correctness_passed(metrics), metrics
 
 
+def test_emulated_scatter_auto_on_cta_pairs():
+    """A row scatter whose K shard is long enough (4096 per rank here) runs on the
+    CTA-pair kernel under `auto`, its rows leaving through the bulk-copy path."""
+    m, hidden, k, world = 4096, 2560, 8192, 2
+    args = capi.make_args(0x1000, 0x1000, 0x1000, m, hidden, k // world, flags=capi.FLAG_OUT_F32, ldc=hidden)
+    rc, cfg, _ = capi.resolve(args)
+    assert rc == capi.OK and cfg in (capi.CFG_PAIR_256x256, capi.CFG_STREAMK_PAIR_256x256), cfg
+    h, w, shards, expect = emulate(m, hidden, k, world, "auto")
+    rows = m // world
+    for q, shard in enumerate(shards):
+        assert torch.equal(shard, expect[q * rows:(q + 1) * rows]), q
+    metrics = oracle.error_metrics(torch.cat(shards), oracle.torch_reference(h, w))
+    assert oracle.correctness_passed(metrics), metrics
+
+
 def test_reduce_slots_scalar_path():
     """Columns not a multiple of 4: the element-wise reduction."""
     g = torch.Generator(device="cuda").manual_seed(1)
