@@ -272,9 +272,8 @@ int hgemm_sm100_read_status(int32_t* value, int clear);
  * the kernels compute themselves (the generic no-TMA tile loader, the operand
  * staging copy, the epilogue's register stores), that it stays inside its
  * matrix. A failed check skips the access, records the first failure and sets
- * HGEMM_SM100_ERR_DEBUG_BOUNDS in the status word; nothing traps. Counterpart
- * of the debug switch the survey of the reference asks for (the reference has
- * none: its kernels are checked by sanitizer runs only).
+ * HGEMM_SM100_ERR_DEBUG_BOUNDS in the status word; nothing traps. The
+ * reference has no such switch: its kernels are checked by sanitizer runs only.
  *
  * hgemm_sm100_debug_build: 1 in a debug build, else 0.
  * hgemm_sm100_debug_read: the first recorded failure of the current device
