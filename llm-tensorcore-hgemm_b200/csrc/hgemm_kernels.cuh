@@ -2148,7 +2148,10 @@ hgemm_pair_streamk_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid
                 tile_coords(sg.tile, tiles_m, tiles_n, p.group_m, tm, tn);
                 const int row0 = tm * 256 + static_cast<int>(rank) * Cfg::kRows;
                 const int col0 = tn * 256 + static_cast<int>(rank) * Cfg::kHalfN;
-                for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+                // Whole tiles walk K backwards on odd waves, as in hgemm_pair_kernel.
+                const bool backwards = sg.tile < T - n_sk && ((sg.tile / G) & 1) != 0;
+                for (int kq = sg.kb0; kq < sg.kb1; ++kq) {
+                    const int kb = backwards ? sg.kb0 + sg.kb1 - 1 - kq : kq;
                     if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, wc)) { ok = false; break; }
                     uint8_t* s_a = smem + stage * Cfg::kStageBytes;
                     uint8_t* s_b = s_a + Cfg::kABytes;

@@ -463,7 +463,7 @@ int check_args(const HgemmSm100Args* a) {
 // reuse in L2 when timed; 8 when none does, e.g. K = 8192).
 int pair_group_m(int32_t cfg, int64_t m, int64_t k, int pairs) {
     int g = 8;
-    if (cfg != HGEMM_SM100_CFG_PAIR_256x256) return g;
+    if (cfg != HGEMM_SM100_CFG_PAIR_256x256 && cfg != HGEMM_SM100_CFG_STREAMK_PAIR_256x256) return g;
     const double panel = 512.0 * static_cast<double>(k);
     for (int h : {16, 32})
         if (h <= cdiv(m, 256) && (h + static_cast<double>(pairs) / h) * panel <= 48e6) g = h;
@@ -954,7 +954,7 @@ int run_core(const HgemmSm100Args& a, int32_t cfg, int32_t split, const DeviceIn
             if ((rc = prepare_store()) != HGEMM_SM100_OK) return rc;
             if ((rc = prepare_kernel(*sp.k, devid)) != HGEMM_SM100_OK) return rc;
             p.streamk = sp.streamk;
-            p.group_m = 8;
+            p.group_m = pair_group_m(cfg, a.m, a.k, dev.sms / 2);
             if (sp.streamk) {
                 if (region == nullptr || region_bytes < sp.bytes) return HGEMM_SM100_ERR_INVALID_ARGUMENT;
                 p.partials = reinterpret_cast<float*>(region);
