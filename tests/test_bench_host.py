@@ -203,3 +203,11 @@ def test_profile_driver_rejects_malformed_cases(case):
                            "--case", "auto:64x64x64", "--case", case], capture_output=True, text=True, timeout=300)
     assert proc.returncode == 2, proc.stderr[-1000:]
     assert "expected IMPL:MxNxK" in proc.stderr
+
+
+def test_profile_driver_rejects_f32_output_for_the_comparator():
+    proc = subprocess.run([sys.executable, str(REPO / "llm-tensorcore-hgemm_b200" / "profile_one.py"),
+                           "--m", "64", "--n", "64", "--k", "64", "--f32-out", "--provider", "cublaslt"],
+                          capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 2, proc.stderr[-1000:]
+    assert "--f32-out applies to this library's kernels only" in proc.stderr
